@@ -1,0 +1,432 @@
+"""Benchmark of the B200 trie-constrained beam search (TBS) engine.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--batch B]
+                    [--impl b200|reference]
+
+A step is one batch of requests (the configuration's batch size per GPU)
+searched against the configuration's synthetic trie.  Default: config 2
+(10M keys, V=500k, K=256, L=16, beam 100, batch 1), the configuration the
+reference's metric is quoted on that fits the default run's time budget.
+
+Arms:
+  b200       value = q/s with inputs resident in HBM (device entry point
+             ft_tbs_batch_device, CUDA events on the launching stream);
+             e2e = q/s through the drop-in `flashtrie.bs_tbs_gpu` with host
+             buffers (H2D of the inputs, D2H of the results inside the timed
+             region); latency mean/p50/p99 per step; roofline of the search
+             kernel against the measured HBM copy bandwidth; cpu_baseline =
+             the reference's own CPU `tbs` on a bounded sample.
+  reference  the reference's CPU `tbs(use_gpu=False)` (the unmodified
+             reference built from its sources by oracle/ref.mk), all host
+             cores, same config/metric.  Rank 0 only.
+
+Multi-GPU (torchrun): the trie is replicated on every rank and each rank
+searches its own batch (weak scaling, no collective on the data path); time
+is the max over ranks.
+"""
+import argparse
+import ctypes
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(REPO, "flash-trie_b200")
+for _p in (REPO, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import workload as W  # noqa: E402
+
+METRIC = "trie-search q/s (latency mean/p99 ms alongside); beam search over the synthetic trie of the named config"
+UNIT = "requests/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", type=int, default=2)
+    ap.add_argument("--batch", type=int, default=0, help="requests per step per GPU (default: the config's)")
+    ap.add_argument("--beam", type=int, default=0, help="override the config's beam width")
+    ap.add_argument("--keys", type=int, default=0, help="override the config's key count (smoke runs only)")
+    ap.add_argument("--requests", type=int, default=64, help="distinct requests cycled through")
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of reference CPU work to time")
+    ap.add_argument("--trie-dir", default="/tmp")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------- setup
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def workload_cfg(args):
+    cfg = dict(W.CONFIGS[args.config])
+    if args.batch:
+        cfg["batch"] = args.batch
+    if args.beam:
+        cfg["beam"] = args.beam
+    if args.keys:
+        cfg["keys"] = args.keys
+    return cfg
+
+
+def trie_path(args, cfg):
+    return os.path.join(args.trie_dir, "ft_bench_c%d_k%d.bin" % (args.config, cfg["keys"]))
+
+
+def make_trie(args, cfg, device):
+    """Generates the config's keys (torch, seeded) and builds the trie with the
+    engine's builder, whose files are byte-identical to the reference
+    builder's.  Returns (path, tokens, offsets, seconds)."""
+    import flashtrie
+    t0 = time.time()
+    tok, off = W.gen_keys_torch(cfg["keys"], cfg["vocab"], cfg["len_lo"], cfg["len_hi"], cfg["zipf"],
+                                seed=args.config, device=device)
+    t = flashtrie.Trie()
+    t.build_flat(tok, off)
+    path = trie_path(args, cfg)
+    t.save(path + ".tmp")
+    os.replace(path + ".tmp", path)
+    np.save(path + ".tok.npy", tok)
+    np.save(path + ".off.npy", off)
+    return path, tok, off, time.time() - t0
+
+
+def load_workload(args, cfg, rank, world, device, barrier):
+    path = trie_path(args, cfg)
+    build_s = 0.0
+    if rank == 0:
+        if not (os.path.exists(path) and os.path.exists(path + ".tok.npy")):
+            path, _, _, build_s = make_trie(args, cfg, device)
+    barrier()
+    tok = np.load(path + ".tok.npy")
+    off = np.load(path + ".off.npy")
+    # Requests: each rank its own seeded slice (weak scaling).
+    n_req = max(args.requests, cfg["batch"])
+    beams, ids, lp = W.gen_requests(args.config, tok, off, n_req, start=rank * n_req, cfg=cfg)
+    return path, tok, off, beams, ids, lp, build_s
+
+
+class Clocks:
+    """Samples SM clocks and throttle reasons with nvidia-smi during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.FIELDS,
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.th = threading.Thread(target=self._read, daemon=True)
+            self.th.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------- C ABI view
+class Params(ctypes.Structure):
+    _fields_ = [("token_logp_threshold", ctypes.c_float), ("reserved", ctypes.c_float),
+                ("sent_logp_threshold", ctypes.c_double), ("length_norm", ctypes.c_double),
+                ("early_exit", ctypes.c_int32), ("reserved2", ctypes.c_int32)]
+
+
+class DeviceBatch(ctypes.Structure):
+    _fields_ = [("n", ctypes.c_uint32), ("num_outpos", ctypes.c_uint32), ("topk", ctypes.c_uint32),
+                ("out_capacity", ctypes.c_uint32)] + [(f, ctypes.c_void_p) for f in
+                                                      ("beams", "topk_id", "topk_logp", "out_count", "out_lpn",
+                                                       "out_len", "out_tok")]
+
+
+def algorithmic_bytes(path, beams, ids, lp, cfg):
+    """Per-request algorithmic bytes from the oracle's byte model (test
+    infrastructure used as the checker/counter only)."""
+    from oracle.oracle import OracleTrie
+    o = OracleTrie(path)
+    out = []
+    for i in range(len(beams)):
+        _, _, st = o.tbs(beams[i], ids[i], lp[i], W.TOKEN_LOGP_THRESHOLD, W.SENT_LOGP_THRESHOLD, W.LENGTH_NORM,
+                         cfg["early_exit"], stats=True)
+        out.append(st.bytes_alg)
+    return np.array(out, dtype=np.float64)
+
+
+def reference_cpu_sample(path, beams, ids, lp, cfg, budget_s, procs=1):
+    """Times the reference CPU tbs on the first requests until budget_s is
+    spent (per process); returns (q/s, per-request ms list, requests, procs)."""
+    if procs <= 1:
+        return _ref_worker((path, beams, ids, lp, cfg["early_exit"], budget_s, 0, 1))
+    import multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(procs) as pool:
+        parts = pool.map(_ref_worker, [(path, beams, ids, lp, cfg["early_exit"], budget_s, r, procs)
+                                       for r in range(procs)])
+    done = sum(p[2] for p in parts)
+    wall = max(p[3] for p in parts)
+    ms = [m for p in parts for m in p[1]]
+    return done / wall if wall > 0 else 0.0, ms, done, wall
+
+
+def _ref_worker(a):
+    path, beams, ids, lp, ee, budget, rank, procs = a
+    os.environ["MARISA_MANAGED_ALLOC"] = "0"
+    sys.path.insert(0, os.path.join(REPO, "oracle", "_ref"))
+    import flashtrie_ref as ref
+    t = ref.Trie()
+    t.mmap(path)
+    ms = []
+    start = time.perf_counter()
+    i = rank
+    while time.perf_counter() - start < budget:
+        j = i % len(beams)
+        a0 = time.perf_counter()
+        ref.tbs(t, beams[j].tolist(), ids[j].tolist(), lp[j].tolist(), W.TOKEN_LOGP_THRESHOLD,
+                W.SENT_LOGP_THRESHOLD, W.LENGTH_NORM, ee, False)
+        ms.append((time.perf_counter() - a0) * 1e3)
+        i += procs
+    wall = time.perf_counter() - start
+    if procs <= 1:
+        return len(ms) / wall, ms, len(ms), wall
+    return None, ms, len(ms), wall
+
+
+# --------------------------------------------------------------- arms
+def run_reference(args, cfg):
+    rank, world, local = dist_env()
+    if rank != 0:
+        return
+    import torch
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    ref_mod = os.path.join(REPO, "oracle", "_ref")
+    if not any(f.startswith("flashtrie_ref") for f in os.listdir(ref_mod) if os.path.isdir(ref_mod)):
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref was not built (reference sources absent)"}))
+        return
+    path, tok, off, beams, ids, lp, _ = load_workload(args, cfg, 0, 1, dev, lambda: None)
+    procs = max(1, min(os.cpu_count() or 1, 64))
+    qps, ms, done, wall = reference_cpu_sample(path, beams, ids, lp, cfg, args.cpu_budget, procs)
+    ms_arr = np.array(ms)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": qps, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": float(ms_arr.mean()) if len(ms) else None,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u32 ids / f64 scores",
+        "data": "synthetic (seeded generator, workload.py)",
+        "config": {"workload": "config%d" % args.config, "keys": cfg["keys"], "vocab": cfg["vocab"],
+                   "K": cfg["K"], "L": cfg["L"], "beam": cfg["beam"], "batch": cfg["batch"],
+                   "early_exit": cfg["early_exit"]},
+        "latency_ms": {"mean": float(ms_arr.mean()) if len(ms) else None,
+                       "p99": float(np.percentile(ms_arr, 99)) if len(ms) else None},
+        "cpu_baseline": {"value": qps, "unit": UNIT, "cores": procs, "kind": "reference",
+                         "sample": "%d requests of config %d in %.1f s wall on %d processes (reference tbs, "
+                                   "use_gpu=False, trie mmap'd)" % (done, args.config, wall, procs)},
+        "e2e": {"value": qps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+
+
+def run_b200(args, cfg):
+    import torch
+    import flashtrie
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+        barrier = lambda: dist.barrier()  # noqa: E731
+    else:
+        barrier = lambda: None  # noqa: E731
+
+    path, tok, off, beams, ids, lp, build_s = load_workload(args, cfg, rank, world, str(dev), barrier)
+    B, L, K, nb = cfg["beam"], cfg["L"], cfg["K"], cfg["batch"]
+    trie = flashtrie.Trie()
+    trie.load(path)
+    t_init = time.time()
+    trie.init_tbs_gpu(nb, max_num_topk=K, max_num_outpos=L, max_num_out_beams=B,
+                      max_num_out_tokens=B * L, max_num_inter_beams=B * L)
+    init_s = time.time() - t_init
+    lib = ctypes.CDLL(os.path.join(PKG, "libftcore.so"))
+    handle = ctypes.c_void_p(trie.ft_handle())
+
+    # Inputs resident in HBM: all distinct requests.
+    R = len(beams)
+    d_beams = torch.from_numpy(beams.astype(np.int32)).to(dev)
+    d_ids = torch.from_numpy(ids.view(np.int32)).to(dev)
+    d_lp = torch.from_numpy(lp).to(dev)
+    out_count = torch.zeros(nb, dtype=torch.int32, device=dev)
+    out_lpn = torch.zeros(nb * B, dtype=torch.float64, device=dev)
+    out_len = torch.zeros(nb * B, dtype=torch.int32, device=dev)
+    out_tok = torch.zeros(nb * B * L, dtype=torch.int32, device=dev)
+    prm = Params(W.TOKEN_LOGP_THRESHOLD, 0.0, W.SENT_LOGP_THRESHOLD, W.LENGTH_NORM, int(cfg["early_exit"]), 0)
+    stream = torch.cuda.Stream(dev)
+    n_slices = max(1, R // nb)
+
+    def launch(step):
+        s = (step % n_slices) * nb
+        b = DeviceBatch(nb, L, K, B, d_beams[s].data_ptr(), d_ids[s].data_ptr(), d_lp[s].data_ptr(),
+                        out_count.data_ptr(), out_lpn.data_ptr(), out_len.data_ptr(), out_tok.data_ptr())
+        rc = lib.ft_tbs_batch_device(handle, ctypes.byref(b), ctypes.byref(prm), ctypes.c_void_p(stream.cuda_stream))
+        if rc != 0:
+            lib.ft_last_error.restype = ctypes.c_char_p
+            raise RuntimeError(lib.ft_last_error().decode())
+
+    with torch.cuda.stream(stream):
+        for s in range(args.warmup):
+            launch(s)
+    torch.cuda.synchronize()
+    st = ctypes.c_uint32()
+    assert lib.ft_trie_device_status(handle, ctypes.byref(st)) == 0 and st.value == 0, "device status %d" % st.value
+
+    clocks = Clocks(local)
+    clocks.start()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for s in range(args.steps):
+        ev[s][0].record(stream)
+        launch(args.warmup + s)
+        ev[s][1].record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    elapsed_ms = t_start.elapsed_time(t_end)
+    step_ms = np.array([a.elapsed_time(b) for a, b in ev])
+    clk = clocks.stop()
+    assert lib.ft_trie_device_status(handle, ctypes.byref(st)) == 0 and st.value == 0, "device status %d" % st.value
+
+    # e2e through the drop-in module with host buffers.
+    e2e_steps = args.steps
+    for s in range(min(args.warmup, 3)):
+        i = (s % n_slices) * nb
+        flashtrie.bs_tbs_gpu(trie, nb, beams[i:i + nb], ids[i:i + nb], lp[i:i + nb], W.TOKEN_LOGP_THRESHOLD,
+                             W.SENT_LOGP_THRESHOLD, W.LENGTH_NORM, cfg["early_exit"])
+    d2h = 0
+    t0 = time.perf_counter()
+    for s in range(e2e_steps):
+        i = (s % n_slices) * nb
+        sents, lpns, _, _ = flashtrie.bs_tbs_gpu(trie, nb, beams[i:i + nb], ids[i:i + nb], lp[i:i + nb],
+                                                 W.TOKEN_LOGP_THRESHOLD, W.SENT_LOGP_THRESHOLD, W.LENGTH_NORM,
+                                                 cfg["early_exit"])
+        d2h += 16 + nb * (4 + 40) + nb * B * (8 + 4 + 4 * L)
+    e2e_s = time.perf_counter() - t0
+    h2d_step = nb * (L * 4 + L * K * 8 + 24) + 8 * (L + 1)
+
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([elapsed_ms, e2e_s], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms, e2e_s = float(t[0]), float(t[1])
+
+    if rank == 0:
+        total_req = args.steps * nb * world
+        value = total_req / (elapsed_ms / 1e3)
+        e2e_value = e2e_steps * nb * world / e2e_s
+        # Roofline of the search kernel: algorithmic bytes per launch over the
+        # launch time (the device call is the row-prep + search kernel pair).
+        used = [((args.warmup + s) % n_slices) * nb for s in range(args.steps)]
+        per_req_bytes = algorithmic_bytes(path, beams[:n_slices * nb], ids[:n_slices * nb], lp[:n_slices * nb], cfg)
+        bytes_per_launch = float(np.mean([per_req_bytes[i:i + nb].sum() for i in used]))
+        peak, peak_kind = measured_peaks()
+        achieved = bytes_per_launch / (float(step_ms.mean()) / 1e3) / 1e9
+        cpu_qps, cpu_ms, cpu_n, cpu_wall = (None, [], 0, 0.0)
+        ref_built = os.path.isdir(os.path.join(REPO, "oracle", "_ref")) and any(
+            f.startswith("flashtrie_ref") for f in os.listdir(os.path.join(REPO, "oracle", "_ref")))
+        if world == 1 and ref_built:
+            cpu_qps, cpu_ms, cpu_n, cpu_wall = reference_cpu_sample(path, beams, ids, lp, cfg, args.cpu_budget, 1)
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u32 ids / f64 scores",
+            "data": "synthetic (seeded generator, workload.py)",
+            "config": {"workload": "config%d" % args.config, "keys": cfg["keys"], "vocab": cfg["vocab"],
+                       "K": cfg["K"], "L": cfg["L"], "beam": B, "batch_per_gpu": nb, "early_exit": cfg["early_exit"],
+                       "parallelism": "replicated trie, batch sharded over %d GPU(s)" % world,
+                       "l2": "not flushed; trie image %.0f MB > 126 MB L2" % (os.path.getsize(path) / 1e6)},
+            "latency_ms": {"mean": float(step_ms.mean()), "p50": float(np.percentile(step_ms, 50)),
+                           "p99": float(np.percentile(step_ms, 99)), "per": "step (batch of %d)" % nb},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(h2d_step),
+                    "d2h_bytes_per_step": int(d2h / max(e2e_steps, 1)),
+                    "path": "flashtrie.bs_tbs_gpu (numpy host buffers)"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None, "peak_source": peak_kind,
+                         "bytes_alg_per_launch": bytes_per_launch},
+            "cpu_baseline": ({"value": cpu_qps, "unit": UNIT, "cores": 1, "kind": "reference",
+                              "sample": "%d requests of config %d, %.1f s, reference tbs(use_gpu=False), 1 core"
+                                        % (cpu_n, args.config, cpu_wall)} if cpu_qps else None),
+            "clocks": clk,
+            "gpu_launches": 2 * args.steps,
+            "setup_s": {"trie_build": build_s, "init_tbs_gpu": init_s},
+        }
+        print(json.dumps(line))
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    cfg = workload_cfg(args)
+    if args.impl == "reference":
+        run_reference(args, cfg)
+    else:
+        run_b200(args, cfg)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,158 @@
+#include <cuda_runtime.h>
+#include <omp.h>
+
+#include <cstring>
+#include <string>
+
+#include "cuda_util.hpp"
+#include "device_trie.hpp"
+
+namespace ftb {
+
+void derive_device_image(const LoudsLevel &lv, HostDeviceImage &out, int num_threads) {
+  if (lv.next) fail(ErrorKind::kState, "MARISA_STATE_ERROR: the GPU search needs a single-trie dictionary (num_tries == 1)");
+  if (lv.node_order() != kLabelOrder)
+    fail(ErrorKind::kState, "MARISA_STATE_ERROR: the GPU search needs a label-ordered trie (MARISA_LABEL_ORDER)");
+  const uint64_t N = lv.num_nodes();
+  if (lv.louds.size < 4 || lv.louds.size != 2 * N + 2 || lv.louds.num_1s != N)
+    fail(ErrorKind::kFormat, "MARISA_FORMAT_ERROR: inconsistent LOUDS bit vector");
+  if (lv.terminal.size < N || lv.link.size < N || lv.bases.size() != N || lv.extras.size < N)
+    fail(ErrorKind::kFormat, "MARISA_FORMAT_ERROR: node arrays shorter than the node count");
+  if (N >= 0xFFFFFFFFull) fail(ErrorKind::kSize, "MARISA_SIZE_ERROR: too many nodes");
+  out.num_nodes = N;
+  out.binary_tail = lv.binary_tail();
+  const uint64_t T = lv.tail.size();
+  if (out.binary_tail) {
+    if (lv.tail_end_flags.size != T || T == 0 || !lv.tail_end_flags.get(T - 1))
+      fail(ErrorKind::kFormat, "MARISA_FORMAT_ERROR: binary tail end flags do not close the tail");
+  } else if (T != 0 && lv.tail[T - 1] != kTailTerminal) {
+    fail(ErrorKind::kFormat, "MARISA_FORMAT_ERROR: text tail does not end with a terminator");
+  }
+
+  // child_begin[n] = select0(n) - n: enumerate the zeros of the LOUDS bits.
+  out.child_begin.assign(N + 1, 0);
+  {
+    uint64_t k = 0;  // zeros seen so far
+    const uint64_t nbits = lv.louds.size;
+    for (uint64_t u = 0; u < lv.louds.units.size() && k <= N; ++u) {
+      uint64_t z = ~lv.louds.units[u];
+      const uint64_t base = u * 64;
+      if (base + 64 > nbits) z &= (nbits - base >= 64) ? ~0ull : ((1ull << (nbits - base)) - 1);
+      while (z && k <= N) {
+        const uint64_t pos = base + (uint64_t)__builtin_ctzll(z);
+        z &= z - 1;
+        out.child_begin[k] = (uint32_t)(pos - k);
+        ++k;
+      }
+    }
+    if (k <= N || out.child_begin[0] != 1 || out.child_begin[N] != N)
+      fail(ErrorKind::kFormat, "MARISA_FORMAT_ERROR: LOUDS child ranges are inconsistent");
+  }
+
+  out.first_label.assign(N, 0);
+  out.link_off.assign(N, 0);
+  out.flags.assign(N, 0);
+  // Link ids are ranks over the link bits; compute per-chunk starting ranks so
+  // the chunks can run in parallel.
+  const uint64_t chunk = 1 << 20;
+  const uint64_t nchunks = (N + chunk - 1) / chunk;
+  std::vector<uint64_t> link_rank(nchunks + 1, 0);
+  for (uint64_t c = 0; c < nchunks; ++c) link_rank[c + 1] = lv.link.rank1(std::min(N, (c + 1) * chunk));
+  if (link_rank[nchunks] > lv.link_extras.size)
+    fail(ErrorKind::kFormat, "MARISA_FORMAT_ERROR: fewer link extras than link nodes");
+  bool bad = false;
+#pragma omp parallel for schedule(dynamic, 1) num_threads(num_threads) reduction(|| : bad)
+  for (int64_t c = 0; c < (int64_t)nchunks; ++c) {
+    uint64_t link_id = link_rank[c];
+    const uint64_t end = std::min(N, (uint64_t)(c + 1) * chunk);
+    for (uint64_t n = (uint64_t)c * chunk; n < end; ++n) {
+      uint8_t f = lv.terminal.get(n) ? kNodeTerminal : 0;
+      if (lv.link.get(n)) {
+        f |= kNodeLink;
+        const uint64_t off = lv.link_offset(n, link_id++);
+        // The kernel reads tail[off] and tail[off + 1] (text) or tail[off]
+        // and the end bit at off (binary); the terminator / end bit that
+        // closes the tail bounds every later step of the walk.
+        if (out.binary_tail ? (off >= T) : (off + 1 >= T)) bad = true;
+        if (off < T) out.first_label[n] = lv.tail[off];
+        out.link_off[n] = (uint32_t)off;
+      } else {
+        out.first_label[n] = lv.label(n);
+      }
+      out.flags[n] = f;
+    }
+  }
+  if (bad) fail(ErrorKind::kFormat, "MARISA_FORMAT_ERROR: link offset outside the tail");
+  // Children of a node must be sorted by first label for the binary search
+  // (label order); reject anything else rather than search it wrongly.
+  bool unsorted = false;
+#pragma omp parallel for schedule(static) num_threads(num_threads) reduction(|| : unsorted)
+  for (int64_t n = 0; n < (int64_t)N; ++n) {
+    const uint32_t b = out.child_begin[n], e = out.child_begin[n + 1];
+    if (e < b || e > N) {
+      unsorted = true;
+      continue;
+    }
+    for (uint32_t c = b + 1; c < e; ++c)
+      if (out.first_label[c - 1] >= out.first_label[c]) unsorted = true;
+  }
+  if (unsorted)
+    fail(ErrorKind::kFormat,
+         "MARISA_FORMAT_ERROR: children are not in ascending label order (the GPU search binary-searches them)");
+}
+
+DeviceTrie::~DeviceTrie() { release(); }
+
+void DeviceTrie::release() {
+  if (device >= 0) {
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(device);
+    cudaFree(child_begin);
+    cudaFree(first_label);
+    cudaFree(link_off);
+    cudaFree(flags);
+    cudaFree(tail);
+    cudaFree(tail_end);
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+  child_begin = first_label = link_off = tail = nullptr;
+  flags = nullptr;
+  tail_end = nullptr;
+  device = -1;
+  bytes = 0;
+}
+
+template <typename T>
+static T *upload_array(const T *src, uint64_t count, uint64_t &bytes) {
+  T *dst = nullptr;
+  const uint64_t b = std::max<uint64_t>(count, 1) * sizeof(T) + 16;  // slack: vectorised tail reads
+  CUDA_TRY(cudaMalloc(&dst, b));
+  CUDA_TRY(cudaMemset(dst, 0, b));
+  if (count) CUDA_TRY(cudaMemcpy(dst, src, count * sizeof(T), cudaMemcpyHostToDevice));
+  bytes += b;
+  return dst;
+}
+
+void DeviceTrie::upload(const LoudsLevel &lv, int num_threads) {
+  HostDeviceImage img;
+  derive_device_image(lv, img, num_threads);
+  release();
+  CUDA_TRY(cudaGetDevice(&device));
+  num_nodes = img.num_nodes;
+  tail_size = lv.tail.size();
+  binary_tail = img.binary_tail;
+  try {
+    child_begin = upload_array(img.child_begin.data(), img.child_begin.size(), bytes);
+    first_label = upload_array(img.first_label.data(), img.first_label.size(), bytes);
+    link_off = upload_array(img.link_off.data(), img.link_off.size(), bytes);
+    flags = upload_array(img.flags.data(), img.flags.size(), bytes);
+    tail = upload_array(lv.tail.data(), lv.tail.size(), bytes);
+    if (binary_tail) tail_end = upload_array(lv.tail_end_flags.units.data(), lv.tail_end_flags.units.size(), bytes);
+  } catch (...) {
+    release();
+    throw;
+  }
+}
+
+}  // namespace ftb

@@ -1,0 +1,67 @@
+// Device image of a trie: the arrays the search kernel gathers from, derived
+// once from the MARISA structures at upload time and never written to disk.
+//
+// The reference kernel walks the succinct structures directly: select0 over
+// the LOUDS bits for a parent's child range (3-5 dependent gathers), rank1 +
+// link_extras + tail to learn a link child's first label inside every binary
+// search probe (lib/marisa/grimoire/trie/tbs-kernels.cu:210-278).  On B200
+// the search is bound by dependent random gathers, so the image spends HBM to
+// make each lookup one sector:
+//   child_begin[n]  u32, n in [0, N]: first child id of node n; the children
+//                   of n are [child_begin[n], child_begin[n+1]) because LOUDS
+//                   numbers siblings consecutively (= select0(n) - n).
+//   first_label[n]  u32: the label of a plain child, or the first tail token
+//                   of a link child, so a child range is one sorted u32 run.
+//   link_off[n]     u32: tail offset of a link node's string (0 otherwise).
+//   flags[n]        u8: bit0 terminal, bit1 link.
+//   tail            u32 cells as stored in the file (0xFFFFFFFF terminates a
+//                   string in a text tail); tail_end: end bits of a binary tail.
+#pragma once
+
+#include <cstdint>
+#include <vector>
+
+#include "../host/marisa_image.hpp"
+
+namespace ftb {
+
+constexpr uint8_t kNodeTerminal = 1;
+constexpr uint8_t kNodeLink = 2;
+
+struct HostDeviceImage {
+  uint64_t num_nodes = 0;
+  std::vector<uint32_t> child_begin;
+  std::vector<uint32_t> first_label;
+  std::vector<uint32_t> link_off;
+  std::vector<uint8_t> flags;
+  bool binary_tail = false;
+};
+
+// Derives and validates the arrays above (throws FormatError on any
+// inconsistency that could send the kernel out of bounds).
+void derive_device_image(const LoudsLevel &lv, HostDeviceImage &out, int num_threads);
+
+// Device-resident trie; owns its allocations.
+struct DeviceTrie {
+  int device = -1;
+  uint64_t num_nodes = 0;
+  uint64_t tail_size = 0;
+  bool binary_tail = false;
+  uint32_t *child_begin = nullptr;
+  uint32_t *first_label = nullptr;
+  uint32_t *link_off = nullptr;
+  uint8_t *flags = nullptr;
+  uint32_t *tail = nullptr;
+  uint64_t *tail_end = nullptr;
+  uint64_t bytes = 0;
+
+  DeviceTrie() = default;
+  DeviceTrie(const DeviceTrie &) = delete;
+  DeviceTrie &operator=(const DeviceTrie &) = delete;
+  ~DeviceTrie();
+  void release();
+  // Uploads the image of `lv` to the current device.
+  void upload(const LoudsLevel &lv, int num_threads);
+};
+
+}  // namespace ftb

@@ -1,0 +1,768 @@
+// Trie-constrained beam search kernels for sm_100a.
+//
+// One CTA owns one request for the whole search (persistent grid, requests
+// strided over CTAs), so a step needs no grid-wide barrier: the reference
+// launches one cooperative grid per request and separates each step's
+// expansion, pruning and history save with 2-3 grid syncs
+// (lib/marisa/grimoire/trie/tbs-kernels.cu:476-594).
+//
+// Per step t of a request:
+//   1. stage row t (ids sorted ascending, their log-probs and original
+//      column indices; sorted once per row by row_prep_kernel) in shared memory;
+//   2. expand:
+//      - in-link beams, one thread each: the next tail cell is the only
+//        allowed token; look it up in the sorted row (tbs-kernels.cu:324-371);
+//      - branching beams, one warp each (dynamic queue): intersect the sorted
+//        child labels [child_begin[n], child_begin[n+1]) with the sorted row,
+//        by scanning the children (small fan-out) or by binary-searching the
+//        children per proposal (large fan-out) (tbs-kernels.cu:210-322);
+//      - thresholds: logp > token_threshold and score + logp > sent_threshold,
+//        compared in f64 (tbs-kernels.cu:229-231);
+//      - children go to the step's candidate list ("next") and, when they end
+//        a key, to the result pool ("selected");
+//   3. select: exact top-beams[t] of the candidates by the pinned order
+//      (logp_norm, node, depth, score), found by an 11-bit MSD radix select over
+//      the 192-bit key; survivors become the next step's beams and append
+//      (parent, token) history records;
+//   4. trim the result pool to the final beam the same way.
+// After the last step the pool is sorted and written ascending with each
+// sequence rebuilt from the history (tbs-kernels.cu:393-474).
+#include <cooperative_groups.h>
+
+#include "cuda_util.hpp"
+#include "tbs_kernel.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace ftb {
+namespace {
+
+constexpr uint32_t kTailTerm = 0xFFFFFFFFu;
+constexpr int kWarps = kSearchThreads / 32;
+constexpr int kRadixBits = 11;
+constexpr int kRadixBins = 1 << kRadixBits;
+constexpr int kKeyBits = 192;
+constexpr int kNodeFlagTerminal = 1;
+constexpr int kNodeFlagLink = 2;
+
+// ------------------------------------------------------------- keys
+// Monotone map of an f64 to u64 (-0.0 folded onto +0.0).
+__device__ __forceinline__ uint64_t orderable(double d) {
+  uint64_t u = (uint64_t)__double_as_longlong(d);
+  if ((u << 1) == 0) u = 0;
+  return (u >> 63) ? ~u : (u | 0x8000000000000000ull);
+}
+
+struct Key3 {
+  uint64_t w[3];  // w[0] most significant
+};
+
+__device__ __forceinline__ Key3 cand_key(const Cand &c, double factor, uint32_t depth) {
+  Key3 k;
+  k.w[0] = orderable(c.score * factor);
+  k.w[1] = ((uint64_t)c.node << 32) | ((uint64_t)(depth & 0xFFFFu) << 16);
+  k.w[2] = orderable(c.score);
+  return k;
+}
+
+__device__ __forceinline__ int key_cmp(const Key3 &a, const Key3 &b) {
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    if (a.w[i] != b.w[i]) return a.w[i] < b.w[i] ? -1 : 1;
+  }
+  return 0;
+}
+
+__device__ __forceinline__ uint64_t low_mask(int width) { return width >= 64 ? ~0ull : ((1ull << width) - 1); }
+
+// `width` bits starting `from_top` bits below the most significant bit.
+__device__ __forceinline__ uint32_t key_bits(const Key3 &k, int from_top, int width) {
+  const int wi = from_top >> 6, o = from_top & 63;
+  const int avail = 64 - o;
+  if (width <= avail) return (uint32_t)((k.w[wi] >> (avail - width)) & low_mask(width));
+  const int rest = width - avail;
+  const uint64_t hi = k.w[wi] & low_mask(avail);
+  const uint64_t lo = k.w[wi + 1] >> (64 - rest);
+  return (uint32_t)((hi << rest) | lo);
+}
+
+__device__ __forceinline__ void key_set_bits(Key3 &k, int from_top, int width, uint64_t v) {
+  const int wi = from_top >> 6, o = from_top & 63;
+  const int avail = 64 - o;
+  if (width <= avail) {
+    const int sh = avail - width;
+    k.w[wi] = (k.w[wi] & ~(low_mask(width) << sh)) | ((v & low_mask(width)) << sh);
+    return;
+  }
+  const int rest = width - avail;
+  k.w[wi] = (k.w[wi] & ~low_mask(avail)) | ((v >> rest) & low_mask(avail));
+  const int sh = 64 - rest;
+  k.w[wi + 1] = (k.w[wi + 1] & ~(low_mask(rest) << sh)) | ((v & low_mask(rest)) << sh);
+}
+
+// --------------------------------------------------------- shared state
+struct SharedState {
+  uint32_t n_in, n_br;          // beams of the current step: in-link / branching
+  uint32_t n_in_new, n_br_new;  // beams being written for the next step
+  uint32_t n_next;              // candidates of this step
+  uint32_t pool_n;              // pool entries kept from earlier steps
+  uint32_t pool_end;            // pool entries after this step's appends
+  uint32_t br_cursor;           // branching-beam queue
+  uint32_t eq_taken;
+  uint32_t cur;                 // current beam buffer
+  uint64_t sel_pushes;          // pushes to the pool so far (early exit)
+  // radix select
+  Key3 sel_prefix;
+  Key3 sel_mask;
+  uint32_t sel_rem;
+  uint32_t sel_digit;
+  uint32_t sel_above;
+  int sel_ge;                   // 1: take every key >= prefix
+  uint32_t warp_sums[kWarps];
+  uint32_t hist[kRadixBins];
+  unsigned long long t_exp, t_sel, t_ovh, t_start;
+};
+
+// Row of the current step, in dynamic shared memory.
+struct RowView {
+  uint32_t *id;
+  float *lp;
+  uint32_t *orig;
+  uint32_t K;
+};
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// First index in the sorted row whose id >= x.
+__device__ __forceinline__ uint32_t row_lower_bound(const RowView &r, uint32_t x) {
+  uint32_t lo = 0, n = r.K;
+  while (n > 0) {
+    const uint32_t half = n >> 1;
+    if (r.id[lo + half] < x) {
+      lo += half + 1;
+      n -= half + 1;
+    } else {
+      n = half;
+    }
+  }
+  return lo;
+}
+
+// Warp-aggregated append: returns this thread's slot.
+__device__ __forceinline__ uint32_t append_slot(uint32_t *counter) {
+  cg::coalesced_group g = cg::coalesced_threads();
+  uint32_t base = 0;
+  if (g.thread_rank() == 0) base = atomicAdd(counter, (uint32_t)g.size());
+  base = g.shfl(base, 0);
+  return base + g.thread_rank();
+}
+
+struct Ctx {
+  const SearchParams *p;
+  SlotView slot;
+  SharedState *S;
+  RowView row;
+  const Beam *cur;
+  uint32_t step;  // t
+};
+
+__device__ __forceinline__ void push_next(const Ctx &c, double score, uint32_t node, uint32_t off, uint32_t parent,
+                                          uint32_t token) {
+  const uint32_t i = append_slot(&c.S->n_next);
+  if (i < c.p->cand_cap) {
+    Cand v;
+    v.score = score;
+    v.node = node;
+    v.aux = off;
+    v.parent = parent;
+    v.token = token;
+    c.slot.next[i] = v;
+  } else {
+    atomicOr(c.p->status, kStatusCandOverflow);
+  }
+}
+
+__device__ __forceinline__ void push_pool(const Ctx &c, double score, uint32_t node, uint32_t parent,
+                                          uint32_t token) {
+  const uint32_t i = append_slot(&c.S->pool_end);
+  if (i < c.p->pool_cap) {
+    Cand v;
+    v.score = score;
+    v.node = node;
+    v.aux = c.step + 1;  // depth
+    v.parent = parent;
+    v.token = token;
+    c.slot.pool[i] = v;
+  } else {
+    atomicOr(c.p->status, kStatusPoolOverflow);
+  }
+}
+
+// Is the string ending at tail cell `off` finished after consuming `off`?
+__device__ __forceinline__ bool tail_ends_at(const TrieView &t, uint32_t off, bool &ok) {
+  if (t.tail_end) {
+    ok = off < t.tail_size;
+    return ok ? ((__ldg(t.tail_end + (off >> 6)) >> (off & 63)) & 1ull) : true;
+  }
+  ok = (uint64_t)off + 1 < t.tail_size;
+  return ok ? (__ldg(t.tail + off + 1) == kTailTerm) : true;
+}
+
+// A child `c` of a branching beam matched proposal log-prob `lp`.
+__device__ __forceinline__ void emit_branch_child(const Ctx &c, const Beam &b, uint32_t parent_idx, uint32_t child,
+                                                  uint32_t label, double score) {
+  const TrieView &t = c.p->trie;
+  const uint8_t f = __ldg(t.flags + child);
+  if (!(f & kNodeFlagLink)) {
+    push_next(c, score, child, kNoOffset, parent_idx, label);
+    if (f & kNodeFlagTerminal) push_pool(c, score, child, parent_idx, label);
+    return;
+  }
+  // Link child: its first tail token was consumed (tbs-kernels.cu:264-268).
+  const uint32_t off = __ldg(t.link_off + child);
+  bool ok;
+  const bool end = tail_ends_at(t, off, ok);
+  if (!ok) {
+    atomicOr(c.p->status, kStatusTailBounds);
+    return;
+  }
+  if (end) {
+    if (f & kNodeFlagTerminal) push_pool(c, score, child, parent_idx, label);
+  } else {
+    push_next(c, score, child, off + 1, parent_idx, label);
+  }
+}
+
+__device__ void expand_inlink(const Ctx &c) {
+  const TrieView &t = c.p->trie;
+  const double tt = c.p->token_threshold, st = c.p->sent_threshold;
+  const uint32_t n_in = c.S->n_in;
+  for (uint32_t i = threadIdx.x; i < n_in; i += blockDim.x) {
+    const Beam b = c.cur[i];
+    const uint32_t off = b.off;
+    if ((uint64_t)off >= t.tail_size || (uint64_t)b.node >= t.num_nodes) {
+      atomicOr(c.p->status, kStatusTailBounds);
+      continue;
+    }
+    const uint32_t tok = __ldg(t.tail + off);
+    bool ok;
+    const bool end = tail_ends_at(t, off, ok);
+    if (!ok) {
+      atomicOr(c.p->status, kStatusTailBounds);
+      continue;
+    }
+    const uint32_t lo = row_lower_bound(c.row, tok);
+    if (lo >= c.row.K || c.row.id[lo] != tok) continue;
+    uint32_t hi = lo + 1;
+    while (hi < c.row.K && c.row.id[hi] == tok) ++hi;
+    for (uint32_t m = lo; m < hi; ++m) {
+      // Duplicate ids: each reference thread keeps its first match only
+      // (matches are in original column order within an equal-id run).
+      bool first = true;
+      for (uint32_t m2 = lo; m2 < m; ++m2)
+        if ((c.row.orig[m2] % kRefBlock) == (c.row.orig[m] % kRefBlock)) first = false;
+      if (!first) continue;
+      const double lp = (double)c.row.lp[m];
+      if (lp <= tt || b.score + lp <= st) continue;
+      const double score = b.score + lp;
+      if (end) {
+        if (__ldg(t.flags + b.node) & kNodeFlagTerminal) push_pool(c, score, b.node, i, tok);
+      } else {
+        push_next(c, score, b.node, off + 1, i, tok);
+      }
+    }
+  }
+}
+
+__device__ void expand_branch(const Ctx &c) {
+  const TrieView &t = c.p->trie;
+  const double tt = c.p->token_threshold, st = c.p->sent_threshold;
+  const uint32_t lane = threadIdx.x & 31;
+  const uint32_t n_br = c.S->n_br;
+  const uint32_t K = c.row.K;
+  const uint32_t beam_cap = c.p->beam_cap;
+  for (;;) {
+    uint32_t q = 0;
+    if (lane == 0) q = atomicAdd(&c.S->br_cursor, 1u);
+    q = __shfl_sync(0xFFFFFFFFu, q, 0);
+    if (q >= n_br) break;
+    const uint32_t idx = beam_cap - 1 - q;
+    const Beam b = c.cur[idx];
+    if ((uint64_t)b.node >= t.num_nodes) {
+      if (lane == 0) atomicOr(c.p->status, kStatusNodeBounds);
+      continue;
+    }
+    const uint32_t c0 = __ldg(t.child_begin + b.node);
+    const uint32_t c1 = __ldg(t.child_begin + b.node + 1);
+    if (c1 <= c0) continue;
+    const uint32_t d = c1 - c0;
+    if (d <= 8u * K + 64u) {
+      // Small fan-out: every child looks its label up in the sorted row.
+      for (uint32_t ch = c0 + lane; ch < c1; ch += 32) {
+        const uint32_t lab = __ldg(t.first_label + ch);
+        uint32_t m = row_lower_bound(c.row, lab);
+        for (; m < K && c.row.id[m] == lab; ++m) {
+          const double lp = (double)c.row.lp[m];
+          if (lp <= tt || b.score + lp <= st) continue;
+          emit_branch_child(c, b, idx, ch, lab, b.score + lp);
+        }
+      }
+    } else {
+      // Large fan-out: every proposal binary-searches the child labels.
+      const uint32_t *labs = t.first_label + c0;
+      for (uint32_t m = lane; m < K; m += 32) {
+        const double lp = (double)c.row.lp[m];
+        if (lp <= tt || b.score + lp <= st) continue;
+        const uint32_t x = c.row.id[m];
+        uint32_t lo = 0, n = d;
+        while (n > 0) {
+          const uint32_t half = n >> 1;
+          if (__ldg(labs + lo + half) < x) {
+            lo += half + 1;
+            n -= half + 1;
+          } else {
+            n = half;
+          }
+        }
+        if (lo < d && __ldg(labs + lo) == x) emit_branch_child(c, b, idx, c0 + lo, x, b.score + lp);
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------- block scans
+__device__ __forceinline__ uint32_t block_exclusive_sum(uint32_t v, SharedState *S) {
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t inc = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+    if (lane >= (uint32_t)o) inc += y;
+  }
+  if (lane == 31) S->warp_sums[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t w = lane < (uint32_t)kWarps ? S->warp_sums[lane] : 0;
+    uint32_t wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, wi, o);
+      if (lane >= (uint32_t)o) wi += y;
+    }
+    if (lane < (uint32_t)kWarps) S->warp_sums[lane] = wi - w;  // exclusive
+  }
+  __syncthreads();
+  const uint32_t r = S->warp_sums[warp] + inc - v;
+  __syncthreads();
+  return r;
+}
+
+// Exact top-k threshold over n candidates by the 192-bit key.  On return
+// S->sel_ge says whether every key >= sel_prefix is taken (exactly k of
+// them), or keys > sel_prefix plus the first sel_rem keys equal to it.
+template <bool kPoolKeys>
+__device__ void radix_select(const Cand *v, uint32_t n, uint32_t k, const double *factor, uint32_t depth_const,
+                             SharedState *S) {
+  if (threadIdx.x == 0) {
+    S->sel_prefix = Key3{{0, 0, 0}};
+    S->sel_mask = Key3{{0, 0, 0}};
+    S->sel_rem = k;
+    S->sel_ge = 0;
+  }
+  __syncthreads();
+  const int passes = (kKeyBits + kRadixBits - 1) / kRadixBits;
+  for (int pass = 0; pass < passes; ++pass) {
+    const int from_top = pass * kRadixBits;
+    const int width = min(kRadixBits, kKeyBits - from_top);
+    for (int b = threadIdx.x; b < kRadixBins; b += blockDim.x) S->hist[b] = 0;
+    __syncthreads();
+    const Key3 P = S->sel_prefix, M = S->sel_mask;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+      const Cand c = v[i];
+      const uint32_t depth = kPoolKeys ? c.aux : depth_const;
+      const Key3 key = cand_key(c, factor[depth], depth);
+      if ((key.w[0] & M.w[0]) == P.w[0] && (key.w[1] & M.w[1]) == P.w[1] && (key.w[2] & M.w[2]) == P.w[2])
+        atomicAdd(&S->hist[key_bits(key, from_top, width)], 1u);
+    }
+    __syncthreads();
+    // Bins from the top: thread i owns bins 2047-4i .. 2044-4i.
+    uint32_t mine[kRadixBins / kSearchThreads];
+    uint32_t sum = 0;
+#pragma unroll
+    for (int q = 0; q < kRadixBins / kSearchThreads; ++q) {
+      mine[q] = S->hist[kRadixBins - 1 - (kRadixBins / kSearchThreads) * threadIdx.x - q];
+      sum += mine[q];
+    }
+    const uint32_t rem = S->sel_rem;
+    const uint32_t above = block_exclusive_sum(sum, S);
+    if (above < rem && rem <= above + sum) {
+      uint32_t acc = above;
+#pragma unroll
+      for (int q = 0; q < kRadixBins / kSearchThreads; ++q) {
+        if (acc + mine[q] >= rem) {
+          S->sel_digit = kRadixBins - 1 - (kRadixBins / kSearchThreads) * threadIdx.x - q;
+          S->sel_above = acc;
+          break;
+        }
+        acc += mine[q];
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const uint32_t d = S->sel_digit;
+      S->sel_rem = rem - S->sel_above;
+      key_set_bits(S->sel_prefix, from_top, width, d);
+      key_set_bits(S->sel_mask, from_top, width, low_mask(width));
+      if (S->hist[d] == S->sel_rem) S->sel_ge = 1;
+    }
+    __syncthreads();
+    if (S->sel_ge) break;
+  }
+  if (threadIdx.x == 0) S->eq_taken = 0;
+  __syncthreads();
+}
+
+// Full-key threshold: keys above it, then the first sel_rem keys equal to it
+// (equal keys are indistinguishable beams, so which ones does not matter).
+__device__ __forceinline__ bool selected(const Key3 &key, SharedState *S) {
+  const int c = key_cmp(key, S->sel_prefix);
+  if (c > 0) return true;
+  if (c < 0) return false;
+  return atomicAdd(&S->eq_taken, 1u) < S->sel_rem;
+}
+
+// Keys with a partial prefix: every key whose masked bits exceed the prefix
+// is above it; compare on the full key with the prefix's free bits at zero.
+__device__ __forceinline__ bool selected_ge(const Key3 &key, const Key3 &prefix) { return key_cmp(key, prefix) >= 0; }
+
+// Makes the selected candidates the beams of step t+1.
+__device__ void materialize_next(const Ctx &c, uint32_t n, uint32_t k, Beam *out_beams) {
+  SharedState *S = c.S;
+  const uint32_t depth = c.step + 1;
+  const double f = c.p->factor[depth];
+  const bool all = n <= k;
+  if (!all && k > 0) radix_select<false>(c.slot.next, n, k, c.p->factor, depth, S);
+  if (k == 0) return;
+  const uint32_t beam_cap = c.p->beam_cap;
+  Hist *hist = c.slot.hist + (uint64_t)depth * beam_cap;
+  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const Cand v = c.slot.next[i];
+    bool take = all;
+    if (!all) {
+      const Key3 key = cand_key(v, f, depth);
+      take = S->sel_ge ? selected_ge(key, S->sel_prefix) : selected(key, S);
+    }
+    if (!take) continue;
+    uint32_t idx;
+    if (v.aux != kNoOffset) {
+      idx = append_slot(&S->n_in_new);
+    } else {
+      idx = beam_cap - 1 - append_slot(&S->n_br_new);
+    }
+    Beam b;
+    b.score = v.score;
+    b.node = v.node;
+    b.off = v.aux;
+    out_beams[idx] = b;
+    hist[idx] = Hist{v.parent, v.token};
+  }
+}
+
+// Trims the pool to the best `k` entries.
+__device__ void trim_pool(const Ctx &c, uint32_t n, uint32_t k) {
+  SharedState *S = c.S;
+  if (n <= k) {
+    if (threadIdx.x == 0) S->pool_n = n;
+    return;
+  }
+  radix_select<true>(c.slot.pool, n, k, c.p->factor, 0, S);
+  if (threadIdx.x == 0) S->n_next = 0;  // reused as the compaction counter
+  __syncthreads();
+  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const Cand v = c.slot.pool[i];
+    const Key3 key = cand_key(v, c.p->factor[v.aux], v.aux);
+    const bool take = S->sel_ge ? selected_ge(key, S->sel_prefix) : selected(key, S);
+    if (take) c.slot.pool_tmp[append_slot(&S->n_next)] = v;
+  }
+  __syncthreads();
+  for (uint32_t i = threadIdx.x; i < k; i += blockDim.x) c.slot.pool[i] = c.slot.pool_tmp[i];
+  if (threadIdx.x == 0) S->pool_n = k;
+}
+
+// Sorts the final pool (descending) and writes the ascending result.
+__device__ void write_result(const SearchParams &p, const SlotView &slot, SharedState *S, uint32_t req,
+                             uint8_t *dyn) {
+  const uint32_t n = S->pool_n;
+  uint32_t P2 = 1;
+  while (P2 < n) P2 <<= 1;
+  ulonglong2 *items = reinterpret_cast<ulonglong2 *>(dyn);
+  for (uint32_t i = threadIdx.x; i < P2; i += blockDim.x) {
+    ulonglong2 it = make_ulonglong2(0, 0);
+    if (i < n) {
+      const Cand v = slot.pool[i];
+      it.x = orderable(v.score * p.factor[v.aux]);
+      it.y = ((uint64_t)v.node << 32) | ((uint64_t)(v.aux & 0xFFFFu) << 16) | (uint64_t)i;
+    }
+    items[i] = it;
+  }
+  __syncthreads();
+  // Bitonic sort, descending.
+  for (uint32_t kk = 2; kk <= P2; kk <<= 1) {
+    for (uint32_t j = kk >> 1; j > 0; j >>= 1) {
+      for (uint32_t i = threadIdx.x; i < P2; i += blockDim.x) {
+        const uint32_t ixj = i ^ j;
+        if (ixj > i) {
+          const ulonglong2 a = items[i], b = items[ixj];
+          const bool a_less = (a.x < b.x) || (a.x == b.x && a.y < b.y);
+          const bool desc = (i & kk) == 0;
+          if (a_less == desc) {
+            items[i] = b;
+            items[ixj] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  const uint32_t cap = p.out_cap, stride = p.out_stride;
+  for (uint32_t s = threadIdx.x; s < n; s += blockDim.x) {
+    const uint32_t idx = (uint32_t)(items[s].y & 0xFFFFu);
+    const Cand v = slot.pool[idx];
+    const uint32_t o = n - 1 - s;
+    const uint64_t slot_o = (uint64_t)req * cap + o;
+    p.out_lpn[slot_o] = v.score * p.factor[v.aux];
+    p.out_len[slot_o] = v.aux;
+    uint32_t *tok = p.out_tok + slot_o * stride;
+    uint32_t depth = v.aux;
+    tok[depth - 1] = v.token;
+    uint32_t j = v.parent;
+    for (uint32_t st = depth - 1; st >= 1; --st) {
+      const Hist h = slot.hist[(uint64_t)st * p.beam_cap + j];
+      tok[st - 1] = h.token;
+      j = h.parent;
+    }
+  }
+  if (threadIdx.x == 0) p.out_count[req] = n;
+}
+
+__device__ void search_request(const SearchParams &p, uint32_t req, const SlotView &slot, SharedState *S,
+                               uint8_t *dyn) {
+  const ReqMeta meta = p.meta[req];
+  const uint32_t L = meta.L, K = meta.K;
+  const uint32_t *beams = p.beams + meta.beams_off;
+  if (threadIdx.x == 0) {
+    S->t_start = global_ns();
+    S->t_exp = S->t_sel = S->t_ovh = 0;
+  }
+  if (L == 0) {
+    if (threadIdx.x == 0) {
+      p.out_count[req] = 0;
+      atomicOr(p.status, kStatusBadRequest);
+    }
+    return;
+  }
+  const uint32_t final_beam = beams[L - 1];
+  if (final_beam == 0) {
+    if (threadIdx.x == 0) p.out_count[req] = 0;
+    return;
+  }
+  // Device-resident batches are not validated on the host: refuse widths
+  // beyond the workspace instead of writing past it.
+  bool bad = final_beam > p.out_cap || L > p.out_stride;
+  for (uint32_t t = threadIdx.x; t < L; t += blockDim.x) bad |= beams[t] > p.beam_cap;
+  if (__syncthreads_or(bad)) {
+    if (threadIdx.x == 0) {
+      p.out_count[req] = 0;
+      atomicOr(p.status, kStatusBadRequest);
+    }
+    return;
+  }
+  const uint32_t beam_cap = p.beam_cap;
+  if (threadIdx.x == 0) {
+    Beam root;
+    root.score = 0.0;
+    root.node = 0;
+    root.off = kNoOffset;
+    slot.beams[0][beam_cap - 1] = root;
+    S->n_in = 0;
+    S->n_br = 1;
+    S->cur = 0;
+    S->pool_n = 0;
+    S->sel_pushes = 0;
+  }
+  RowView row;
+  row.id = reinterpret_cast<uint32_t *>(dyn);
+  row.lp = reinterpret_cast<float *>(dyn + sizeof(uint32_t) * K);
+  row.orig = reinterpret_cast<uint32_t *>(dyn + 2 * sizeof(uint32_t) * K);
+  row.K = K;
+  __syncthreads();
+
+  for (uint32_t t = 0; t < L; ++t) {
+    unsigned long long t0 = 0;
+    if (threadIdx.x == 0) t0 = global_ns();
+    if (S->n_in + S->n_br == 0 || (p.early_exit && S->sel_pushes >= final_beam)) break;
+    const uint64_t rbase = meta.rows_off + (uint64_t)t * K;
+    for (uint32_t j = threadIdx.x; j < K; j += blockDim.x) {
+      row.id[j] = p.row_id[rbase + j];
+      row.lp[j] = p.row_lp[rbase + j];
+      row.orig[j] = p.row_orig[rbase + j];
+    }
+    if (threadIdx.x == 0) {
+      S->n_next = 0;
+      S->pool_end = S->pool_n;
+      S->br_cursor = 0;
+      S->n_in_new = 0;
+      S->n_br_new = 0;
+    }
+    __syncthreads();
+    unsigned long long t1 = 0;
+    if (threadIdx.x == 0) t1 = global_ns();
+
+    Ctx c;
+    c.p = &p;
+    c.slot = slot;
+    c.S = S;
+    c.row = row;
+    c.cur = slot.beams[S->cur];
+    c.step = t;
+    expand_inlink(c);
+    expand_branch(c);
+    __syncthreads();
+    unsigned long long t2 = 0;
+    if (threadIdx.x == 0) t2 = global_ns();
+
+    const uint32_t n_next = min(S->n_next, (uint32_t)p.cand_cap);
+    const uint32_t pool_end = min(S->pool_end, (uint32_t)p.pool_cap);
+    const uint32_t pool_before = S->pool_n;
+    __syncthreads();
+    materialize_next(c, n_next, beams[t], slot.beams[S->cur ^ 1]);
+    __syncthreads();
+    trim_pool(c, pool_end, final_beam);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      S->sel_pushes += (uint64_t)(pool_end - pool_before);
+      S->n_in = S->n_in_new;
+      S->n_br = S->n_br_new;
+      S->cur ^= 1;
+      const unsigned long long t3 = global_ns();
+      S->t_ovh += t1 - t0;
+      S->t_exp += t2 - t1;
+      S->t_sel += t3 - t2;
+    }
+    __syncthreads();
+  }
+  unsigned long long t4 = 0;
+  if (threadIdx.x == 0) t4 = global_ns();
+  write_result(p, slot, S, req, dyn);
+  if (threadIdx.x == 0 && p.out_phase_ms) {
+    const unsigned long long t5 = global_ns();
+    double *ph = p.out_phase_ms + (uint64_t)req * 5;
+    ph[0] = S->t_exp * 1e-6;
+    ph[1] = 0.0;  // validation is fused into expansion
+    ph[2] = S->t_sel * 1e-6;
+    ph[3] = (S->t_ovh + (t5 - t4)) * 1e-6;
+    ph[4] = (t5 - S->t_start) * 1e-6;
+  }
+}
+
+__global__ void __launch_bounds__(kSearchThreads, 1) tbs_search_kernel(const SearchParams p) {
+  extern __shared__ __align__(16) uint8_t dyn[];
+  __shared__ SharedState S;
+  const SlotView slot = p.slots[blockIdx.x];
+  for (uint32_t req = blockIdx.x; req < p.n_req; req += gridDim.x) {
+    search_request(p, req, slot, &S, dyn);
+    __syncthreads();
+  }
+}
+
+// Sorts each row by (id, original column) so the search can binary-search it;
+// rows that are already strictly ascending are copied as they are.
+__global__ void row_prep_kernel(const ReqMeta *meta, const uint32_t *ids, const float *lps, uint32_t *out_id,
+                                float *out_lp, uint32_t *out_orig, uint32_t n_req) {
+  extern __shared__ __align__(16) uint8_t dyn[];
+  uint64_t *keys = reinterpret_cast<uint64_t *>(dyn);
+  const uint32_t r = blockIdx.y, t = blockIdx.x;
+  if (r >= n_req) return;
+  const ReqMeta m = meta[r];
+  if (t >= m.L) return;
+  const uint32_t K = m.K;
+  const uint64_t base = m.rows_off + (uint64_t)t * K;
+  bool ok = true;
+  for (uint32_t j = threadIdx.x; j + 1 < K; j += blockDim.x)
+    if (ids[base + j] >= ids[base + j + 1]) ok = false;
+  if (__syncthreads_and(ok)) {
+    for (uint32_t j = threadIdx.x; j < K; j += blockDim.x) {
+      out_id[base + j] = ids[base + j];
+      out_lp[base + j] = lps[base + j];
+      out_orig[base + j] = j;
+    }
+    return;
+  }
+  uint32_t P2 = 1;
+  while (P2 < K) P2 <<= 1;
+  for (uint32_t j = threadIdx.x; j < P2; j += blockDim.x)
+    keys[j] = j < K ? (((uint64_t)ids[base + j] << 32) | j) : ~0ull;
+  __syncthreads();
+  for (uint32_t kk = 2; kk <= P2; kk <<= 1) {
+    for (uint32_t j = kk >> 1; j > 0; j >>= 1) {
+      for (uint32_t i = threadIdx.x; i < P2; i += blockDim.x) {
+        const uint32_t ixj = i ^ j;
+        if (ixj > i) {
+          const uint64_t a = keys[i], b = keys[ixj];
+          const bool up = (i & kk) == 0;
+          if ((a > b) == up) {
+            keys[i] = b;
+            keys[ixj] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (uint32_t j = threadIdx.x; j < K; j += blockDim.x) {
+    const uint32_t o = (uint32_t)(keys[j] & 0xFFFFFFFFu);
+    out_id[base + j] = (uint32_t)(keys[j] >> 32);
+    out_lp[base + j] = lps[base + o];
+    out_orig[base + j] = o;
+  }
+}
+
+}  // namespace
+
+size_t search_smem_bytes(uint32_t max_topk, uint32_t max_final_beam) {
+  uint32_t P2 = 1;
+  while (P2 < max_final_beam) P2 <<= 1;
+  const size_t row = (size_t)max_topk * 12;
+  const size_t sort = (size_t)P2 * 16;
+  return std::max<size_t>(std::max(row, sort), 16);
+}
+
+int configure_search_kernel(size_t smem_bytes) {
+  CUDA_TRY(cudaFuncSetAttribute(tbs_search_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes));
+  CUDA_TRY(cudaFuncSetAttribute(row_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024));
+  int per_sm = 0;
+  CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tbs_search_kernel, kSearchThreads, smem_bytes));
+  int dev = 0, sms = 0;
+  CUDA_TRY(cudaGetDevice(&dev));
+  CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  return std::max(per_sm, 1) * sms;
+}
+
+void launch_search(const SearchParams &p, uint32_t max_K, uint32_t max_L, size_t smem_bytes, int grid,
+                   cudaStream_t stream) {
+  if (p.n_req == 0) return;
+  uint32_t P2 = 1;
+  while (P2 < max_K) P2 <<= 1;
+  dim3 pg(max_L, p.n_req);
+  row_prep_kernel<<<pg, 256, (size_t)P2 * 8, stream>>>(p.meta, p.topk_id, p.topk_logp, p.row_id, p.row_lp,
+                                                       p.row_orig, p.n_req);
+  CUDA_TRY(cudaGetLastError());
+  tbs_search_kernel<<<grid, kSearchThreads, smem_bytes, stream>>>(p);
+  CUDA_TRY(cudaGetLastError());
+}
+
+}  // namespace ftb

@@ -1,0 +1,120 @@
+// Shared declarations of the TBS search kernels (device side) and the host
+// launcher.  See tbs_kernel.cu for the algorithm.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace ftb {
+
+constexpr uint32_t kNoOffset = 0xFFFFFFFFu;  // Beam::off of a beam not inside a link
+constexpr int kSearchThreads = 512;          // threads per search CTA
+constexpr int kRefBlock = 512;               // threads per CTA of the reference kernel
+                                             // (tbs-kernels.cu:10): in-link matches are
+                                             // taken first-per-residue-class of this size
+
+// Candidate produced by expansion (24 bytes).
+//   next-candidates: aux = tail offset of the next token (kNoOffset if none)
+//   pool entries:    aux = depth
+struct Cand {
+  double score;
+  uint32_t node;
+  uint32_t aux;
+  uint32_t parent;  // index of the parent beam in the step's beam array
+  uint32_t token;
+};
+
+// A live beam (16 bytes).
+struct Beam {
+  double score;
+  uint32_t node;
+  uint32_t off;  // next tail cell for an in-link beam, kNoOffset otherwise
+};
+
+// History record of the beam at index i of step s: its parent's index at
+// step s-1 and its last token.
+struct Hist {
+  uint32_t parent;
+  uint32_t token;
+};
+
+// Per-request metadata (element offsets into the packed batch arrays).
+struct ReqMeta {
+  uint32_t L;
+  uint32_t K;
+  uint64_t beams_off;  // into beams[]
+  uint64_t rows_off;   // into topk_id[] / topk_logp[] and the sorted-row workspace
+};
+
+struct TrieView {
+  const uint32_t *child_begin;
+  const uint32_t *first_label;
+  const uint32_t *link_off;
+  const uint8_t *flags;
+  const uint32_t *tail;
+  const uint64_t *tail_end;  // nullptr for a text tail
+  uint64_t num_nodes;
+  uint64_t tail_size;
+};
+
+// Device workspace of one search slot (one in-flight request).
+struct SlotView {
+  Cand *next;        // [cand_cap]
+  Cand *pool;        // [pool_cap]
+  Cand *pool_tmp;    // [beam_cap]
+  Beam *beams[2];    // [beam_cap] each
+  Hist *hist;        // [(max_outpos + 1) * beam_cap]
+};
+
+struct SearchParams {
+  TrieView trie;
+  const ReqMeta *meta;
+  const uint32_t *beams;
+  const uint32_t *topk_id;
+  const float *topk_logp;
+  const double *factor;     // [max L + 1]: (6 / (5 + depth)) ^ length_norm
+  // sorted rows (written by the row-prep kernel)
+  uint32_t *row_id;
+  float *row_lp;
+  uint32_t *row_orig;
+  // workspace
+  SlotView *slots;
+  uint64_t cand_cap;
+  uint64_t pool_cap;
+  uint32_t beam_cap;
+  uint32_t n_req;
+  uint32_t n_slots;
+  // search parameters
+  double token_threshold;
+  double sent_threshold;
+  int early_exit;
+  // outputs
+  uint32_t out_cap;
+  uint32_t out_stride;
+  uint32_t *out_count;
+  double *out_lpn;
+  uint32_t *out_len;
+  uint32_t *out_tok;
+  double *out_phase_ms;  // [n_req][5] or nullptr
+  uint32_t *status;      // device status word (bit flags, see kStatus*)
+};
+
+constexpr uint32_t kStatusCandOverflow = 1u;
+constexpr uint32_t kStatusPoolOverflow = 2u;
+constexpr uint32_t kStatusTailBounds = 4u;
+constexpr uint32_t kStatusNodeBounds = 8u;
+constexpr uint32_t kStatusBadRequest = 16u;
+
+// Shared-memory bytes the search kernel needs for a given max K / max final beam.
+size_t search_smem_bytes(uint32_t max_topk, uint32_t max_final_beam);
+
+// Enqueues the row-prep kernel and the search kernel on `stream`.
+// `max_K`, `max_L` bound every request of the batch.
+void launch_search(const SearchParams &p, uint32_t max_K, uint32_t max_L, size_t smem_bytes, int grid,
+                   cudaStream_t stream);
+
+// Configures kernel attributes once per device; returns max resident search CTAs.
+int configure_search_kernel(size_t smem_bytes);
+
+}  // namespace ftb

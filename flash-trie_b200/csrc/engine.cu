@@ -1,0 +1,291 @@
+#include "engine.hpp"
+
+#include <cmath>
+#include <cstring>
+#include <string>
+
+#include "device/cuda_util.hpp"
+
+namespace ftb {
+
+namespace {
+
+inline size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
+
+// (6 / (5 + depth)) ^ length_norm for depth 0..max_L, computed on the host so
+// device scores are bit-identical to a host computation of the reference
+// formula (lib/marisa/grimoire/trie/beam-state.h:24-26).
+void fill_factor(double *f, uint32_t max_L, double length_norm) {
+  for (uint32_t d = 0; d <= max_L; ++d) f[d] = std::pow(6.0 / (5.0 + (double)d), length_norm);
+}
+
+}  // namespace
+
+void *Engine::dalloc(size_t bytes) {
+  void *p = nullptr;
+  bytes = std::max<size_t>(align16(bytes), 16);
+  CUDA_TRY(cudaMalloc(&p, bytes));
+  allocs_.push_back(DevBuf{p, bytes});
+  return p;
+}
+
+Engine::Engine(std::shared_ptr<DeviceTrie> trie, const EngineLimits &lim) : trie_(std::move(trie)), lim_(lim) {
+  if (lim.max_batch == 0) throw InvalidArgument("init_tbs_gpu: max_batch_size must be >= 1");
+  if (lim.max_topk == 0 || lim.max_topk > kMaxTopk)
+    throw InvalidArgument("init_tbs_gpu: max_num_topk must be in [1, " + std::to_string(kMaxTopk) + "]");
+  if (lim.max_outpos == 0 || lim.max_outpos > kMaxOutpos)
+    throw InvalidArgument("init_tbs_gpu: max_num_outpos must be in [1, " + std::to_string(kMaxOutpos) + "]");
+  if (lim.max_out_beams == 0 || lim.max_out_beams > kMaxBeams)
+    throw InvalidArgument("init_tbs_gpu: max_num_out_beams must be in [1, " + std::to_string(kMaxBeams) + "]");
+  CUDA_TRY(cudaGetDevice(&device_));
+  smem_ = search_smem_bytes((uint32_t)lim.max_topk, (uint32_t)lim.max_out_beams);
+  max_ctas_ = configure_search_kernel(smem_);
+  n_slots_ = (uint32_t)std::min<uint64_t>(lim.max_batch, (uint64_t)max_ctas_);
+
+  const uint64_t B = lim.max_out_beams, K = lim.max_topk, L = lim.max_outpos, NB = lim.max_batch;
+  const uint64_t cand_cap = B * K, pool_cap = B + B * K;
+  try {
+    std::vector<SlotView> slots(n_slots_);
+    for (uint32_t s = 0; s < n_slots_; ++s) {
+      slots[s].next = (Cand *)dalloc(sizeof(Cand) * cand_cap);
+      slots[s].pool = (Cand *)dalloc(sizeof(Cand) * pool_cap);
+      slots[s].pool_tmp = (Cand *)dalloc(sizeof(Cand) * B);
+      slots[s].beams[0] = (Beam *)dalloc(sizeof(Beam) * B);
+      slots[s].beams[1] = (Beam *)dalloc(sizeof(Beam) * B);
+      slots[s].hist = (Hist *)dalloc(sizeof(Hist) * (L + 1) * B);
+    }
+    d_slots_ = (SlotView *)dalloc(sizeof(SlotView) * n_slots_);
+    CUDA_TRY(cudaMemcpy(d_slots_, slots.data(), sizeof(SlotView) * n_slots_, cudaMemcpyHostToDevice));
+    d_row_id_ = (uint32_t *)dalloc(4 * NB * L * K);
+    d_row_lp_ = (float *)dalloc(4 * NB * L * K);
+    d_row_orig_ = (uint32_t *)dalloc(4 * NB * L * K);
+    d_status_ = (uint32_t *)dalloc(16);
+    CUDA_TRY(cudaMemset(d_status_, 0, 16));
+
+    in_bytes_ = align16(sizeof(ReqMeta) * NB) + align16(8 * (L + 1)) + align16(4 * NB * L) + 2 * align16(4 * NB * L * K);
+    d_in_ = (uint8_t *)dalloc(in_bytes_);
+    CUDA_TRY(cudaMallocHost(&h_in_, in_bytes_));
+    out_bytes_ = 16 + align16(4 * NB) + align16(8 * 5 * NB) + align16(8 * NB * B) + align16(4 * NB * B) +
+                 align16(4 * NB * B * L);
+    d_out_ = (uint8_t *)dalloc(out_bytes_);
+    CUDA_TRY(cudaMallocHost(&h_out_, out_bytes_));
+    dmeta_bytes_ = align16(sizeof(ReqMeta) * NB) + align16(8 * (L + 1));
+    d_dmeta_ = (uint8_t *)dalloc(dmeta_bytes_);
+    CUDA_TRY(cudaMallocHost(&h_dmeta_, dmeta_bytes_));
+    CUDA_TRY(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    CUDA_TRY(cudaEventCreateWithFlags(&dmeta_done_, cudaEventDisableTiming));
+  } catch (...) {
+    release();
+    throw;
+  }
+}
+
+Engine::~Engine() { release(); }
+
+void Engine::release() {
+  int prev = -1;
+  cudaGetDevice(&prev);
+  if (device_ >= 0) cudaSetDevice(device_);
+  if (stream_) cudaStreamSynchronize(stream_);
+  for (auto &a : allocs_) cudaFree(a.p);
+  allocs_.clear();
+  if (h_in_) cudaFreeHost(h_in_);
+  if (h_out_) cudaFreeHost(h_out_);
+  if (h_dmeta_) cudaFreeHost(h_dmeta_);
+  if (dmeta_done_) cudaEventDestroy(dmeta_done_);
+  if (stream_) cudaStreamDestroy(stream_);
+  h_in_ = h_out_ = h_dmeta_ = nullptr;
+  stream_ = nullptr;
+  dmeta_done_ = nullptr;
+  if (prev >= 0) cudaSetDevice(prev);
+}
+
+void Engine::validate_request(const ft_request &r) const {
+  if (r.num_outpos == 0) throw InvalidArgument("tbs: beams must not be empty");
+  if (r.num_outpos > lim_.max_outpos)
+    throw InvalidArgument("tbs: len(beams) = " + std::to_string(r.num_outpos) + " exceeds max_num_outpos = " +
+                          std::to_string(lim_.max_outpos));
+  if (r.topk > lim_.max_topk)
+    throw InvalidArgument("tbs: top-k row length " + std::to_string(r.topk) + " exceeds max_num_topk = " +
+                          std::to_string(lim_.max_topk));
+  for (uint32_t t = 0; t < r.num_outpos; ++t)
+    if (r.beams[t] > lim_.max_out_beams)
+      throw InvalidArgument("tbs: beam width " + std::to_string(r.beams[t]) + " exceeds max_num_out_beams = " +
+                            std::to_string(lim_.max_out_beams));
+}
+
+void Engine::fill_params(SearchParams &sp, const ft_search_params &prm, uint32_t n_req) const {
+  std::memset(&sp, 0, sizeof(sp));
+  const DeviceTrie &t = *trie_;
+  sp.trie.child_begin = t.child_begin;
+  sp.trie.first_label = t.first_label;
+  sp.trie.link_off = t.link_off;
+  sp.trie.flags = t.flags;
+  sp.trie.tail = t.tail;
+  sp.trie.tail_end = t.binary_tail ? t.tail_end : nullptr;
+  sp.trie.num_nodes = t.num_nodes;
+  sp.trie.tail_size = t.tail_size;
+  sp.row_id = d_row_id_;
+  sp.row_lp = d_row_lp_;
+  sp.row_orig = d_row_orig_;
+  sp.slots = d_slots_;
+  sp.cand_cap = lim_.max_out_beams * lim_.max_topk;
+  sp.pool_cap = lim_.max_out_beams + lim_.max_out_beams * lim_.max_topk;
+  sp.beam_cap = (uint32_t)lim_.max_out_beams;
+  sp.n_req = n_req;
+  sp.n_slots = n_slots_;
+  // The reference binds token_logp_threshold as float and compares it as a
+  // double (tools/bindings.cpp:50, beam-search-state.h:158).
+  sp.token_threshold = (double)prm.token_logp_threshold;
+  sp.sent_threshold = prm.sent_logp_threshold;
+  sp.early_exit = prm.early_exit ? 1 : 0;
+  sp.status = d_status_;
+}
+
+void Engine::search_host(const ft_request *reqs, uint32_t n, const ft_search_params &prm, ft_result *out) {
+  std::lock_guard<std::mutex> lock(mu_);
+  if (n > lim_.max_batch)
+    throw InvalidArgument("bs_tbs_gpu: batch_size " + std::to_string(n) + " exceeds max_batch_size = " +
+                          std::to_string(lim_.max_batch));
+  uint32_t max_L = 0, max_K = 1, cap = 1;
+  uint64_t sum_L = 0, sum_LK = 0;
+  for (uint32_t i = 0; i < n; ++i) {
+    validate_request(reqs[i]);
+    if (out[i].capacity < reqs[i].beams[reqs[i].num_outpos - 1] || out[i].stride < reqs[i].num_outpos)
+      throw InvalidArgument("tbs: result buffer too small");
+    max_L = std::max(max_L, reqs[i].num_outpos);
+    max_K = std::max(max_K, reqs[i].topk);
+    cap = std::max(cap, reqs[i].beams[reqs[i].num_outpos - 1]);
+    sum_L += reqs[i].num_outpos;
+    sum_LK += (uint64_t)reqs[i].num_outpos * reqs[i].topk;
+  }
+  for (uint32_t i = 0; i < n; ++i) {
+    out[i].num_beams = 0;
+    for (int k = 0; k < 5; ++k) out[i].phase_ms[k] = 0.0;
+  }
+  if (n == 0) return;
+  CUDA_TRY(cudaSetDevice(device_));
+
+  // Pack [meta | factor | beams | ids | logp] into pinned memory.
+  const size_t o_meta = 0, o_fac = align16(sizeof(ReqMeta) * n), o_beams = o_fac + align16(8 * (max_L + 1)),
+               o_ids = o_beams + align16(4 * sum_L), o_lp = o_ids + align16(4 * sum_LK),
+               in_used = o_lp + align16(4 * sum_LK);
+  ReqMeta *meta = reinterpret_cast<ReqMeta *>(h_in_ + o_meta);
+  fill_factor(reinterpret_cast<double *>(h_in_ + o_fac), max_L, prm.length_norm);
+  uint32_t *hb = reinterpret_cast<uint32_t *>(h_in_ + o_beams);
+  uint32_t *hid = reinterpret_cast<uint32_t *>(h_in_ + o_ids);
+  float *hlp = reinterpret_cast<float *>(h_in_ + o_lp);
+  uint64_t bo = 0, ro = 0;
+  for (uint32_t i = 0; i < n; ++i) {
+    const ft_request &r = reqs[i];
+    meta[i] = ReqMeta{r.num_outpos, r.topk, bo, ro};
+    std::memcpy(hb + bo, r.beams, 4ull * r.num_outpos);
+    const uint64_t lk = (uint64_t)r.num_outpos * r.topk;
+    if (lk) {
+      std::memcpy(hid + ro, r.topk_id, 4 * lk);
+      std::memcpy(hlp + ro, r.topk_logp, 4 * lk);
+    }
+    bo += r.num_outpos;
+    ro += lk;
+  }
+  CUDA_TRY(cudaMemcpyAsync(d_in_, h_in_, in_used, cudaMemcpyHostToDevice, stream_));
+
+  // Output region [status | count | phase | lpn | len | tok] for this batch.
+  const uint32_t stride = max_L;
+  const size_t q_count = 16, q_phase = q_count + align16(4 * n), q_lpn = q_phase + align16(8 * 5 * n),
+               q_len = q_lpn + align16(8ull * n * cap), q_tok = q_len + align16(4ull * n * cap),
+               out_used = q_tok + align16(4ull * n * cap * stride);
+  CUDA_TRY(cudaMemsetAsync(d_status_, 0, 4, stream_));
+
+  SearchParams sp;
+  fill_params(sp, prm, n);
+  sp.meta = reinterpret_cast<const ReqMeta *>(d_in_ + o_meta);
+  sp.factor = reinterpret_cast<const double *>(d_in_ + o_fac);
+  sp.beams = reinterpret_cast<const uint32_t *>(d_in_ + o_beams);
+  sp.topk_id = reinterpret_cast<const uint32_t *>(d_in_ + o_ids);
+  sp.topk_logp = reinterpret_cast<const float *>(d_in_ + o_lp);
+  sp.out_cap = cap;
+  sp.out_stride = stride;
+  sp.out_count = reinterpret_cast<uint32_t *>(d_out_ + q_count);
+  sp.out_phase_ms = reinterpret_cast<double *>(d_out_ + q_phase);
+  sp.out_lpn = reinterpret_cast<double *>(d_out_ + q_lpn);
+  sp.out_len = reinterpret_cast<uint32_t *>(d_out_ + q_len);
+  sp.out_tok = reinterpret_cast<uint32_t *>(d_out_ + q_tok);
+  const int grid = (int)std::min<uint32_t>(n, n_slots_);
+  launch_search(sp, max_K, max_L, smem_, grid, stream_);
+  CUDA_TRY(cudaMemcpyAsync(d_out_, d_status_, 4, cudaMemcpyDeviceToDevice, stream_));
+  CUDA_TRY(cudaMemcpyAsync(h_out_, d_out_, out_used, cudaMemcpyDeviceToHost, stream_));
+  CUDA_TRY(cudaStreamSynchronize(stream_));
+
+  const uint32_t status = *reinterpret_cast<const uint32_t *>(h_out_);
+  if (status != 0)
+    throw std::runtime_error("tbs: the search kernel reported a failed bounds check (status 0x" +
+                             std::to_string(status) + "); the trie image or workspace is inconsistent");
+  const uint32_t *hcount = reinterpret_cast<const uint32_t *>(h_out_ + q_count);
+  const double *hphase = reinterpret_cast<const double *>(h_out_ + q_phase);
+  const double *hlpn = reinterpret_cast<const double *>(h_out_ + q_lpn);
+  const uint32_t *hlen = reinterpret_cast<const uint32_t *>(h_out_ + q_len);
+  const uint32_t *htok = reinterpret_cast<const uint32_t *>(h_out_ + q_tok);
+  for (uint32_t i = 0; i < n; ++i) {
+    const uint32_t nb = hcount[i];
+    ft_result &r = out[i];
+    r.num_beams = nb;
+    for (int k = 0; k < 5; ++k) r.phase_ms[k] = hphase[5 * i + k];
+    for (uint32_t b = 0; b < nb; ++b) {
+      const uint64_t s = (uint64_t)i * cap + b;
+      r.logp_norm[b] = hlpn[s];
+      const uint32_t len = hlen[s];
+      r.lengths[b] = len;
+      std::memcpy(r.tokens + (uint64_t)b * r.stride, htok + s * stride, 4ull * len);
+    }
+  }
+}
+
+void Engine::search_device(const ft_device_batch &b, const ft_search_params &prm, cudaStream_t stream) {
+  std::lock_guard<std::mutex> lock(mu_);
+  if (b.n > lim_.max_batch)
+    throw InvalidArgument("batch of " + std::to_string(b.n) + " exceeds max_batch_size = " +
+                          std::to_string(lim_.max_batch));
+  if (b.num_outpos == 0 || b.num_outpos > lim_.max_outpos || b.topk > lim_.max_topk)
+    throw InvalidArgument("device batch shape exceeds the workspace limits");
+  if (b.n == 0) return;
+  CUDA_TRY(cudaSetDevice(device_));
+  const uint32_t L = b.num_outpos, K = b.topk;
+  // The pinned meta buffer may still feed the previous call's copy.
+  CUDA_TRY(cudaEventSynchronize(dmeta_done_));
+  ReqMeta *meta = reinterpret_cast<ReqMeta *>(h_dmeta_);
+  const size_t o_fac = align16(sizeof(ReqMeta) * b.n);
+  for (uint32_t i = 0; i < b.n; ++i) meta[i] = ReqMeta{L, K, (uint64_t)i * L, (uint64_t)i * L * K};
+  fill_factor(reinterpret_cast<double *>(h_dmeta_ + o_fac), L, prm.length_norm);
+  CUDA_TRY(cudaMemcpyAsync(d_dmeta_, h_dmeta_, o_fac + 8 * (L + 1), cudaMemcpyHostToDevice, stream));
+  CUDA_TRY(cudaEventRecord(dmeta_done_, stream));
+
+  SearchParams sp;
+  fill_params(sp, prm, b.n);
+  sp.meta = reinterpret_cast<const ReqMeta *>(d_dmeta_);
+  sp.factor = reinterpret_cast<const double *>(d_dmeta_ + o_fac);
+  sp.beams = b.beams;
+  sp.topk_id = b.topk_id;
+  sp.topk_logp = b.topk_logp;
+  sp.out_cap = b.out_capacity;
+  sp.out_stride = L;
+  sp.out_count = b.out_count;
+  sp.out_lpn = b.out_lpn;
+  sp.out_len = b.out_len;
+  sp.out_tok = b.out_tok;
+  sp.out_phase_ms = nullptr;
+  const int grid = (int)std::min<uint32_t>(b.n, n_slots_);
+  CUDA_TRY(cudaMemsetAsync(d_status_, 0, 4, stream));
+  launch_search(sp, K, L, smem_, grid, stream);
+}
+
+uint32_t Engine::read_status() {
+  std::lock_guard<std::mutex> lock(mu_);
+  uint32_t s = 0;
+  CUDA_TRY(cudaSetDevice(device_));
+  CUDA_TRY(cudaDeviceSynchronize());
+  CUDA_TRY(cudaMemcpy(&s, d_status_, 4, cudaMemcpyDeviceToHost));
+  return s;
+}
+
+}  // namespace ftb

@@ -1,0 +1,93 @@
+// Search engine: owns the device workspace sized by init_tbs_gpu and runs
+// batches either from host buffers (packing, one H2D copy, kernels, one D2H
+// copy) or from device-resident buffers on a caller stream.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <memory>
+#include <mutex>
+#include <vector>
+
+#include "../../include/flashtrie_b200.h"
+#include "device/device_trie.hpp"
+#include "device/tbs_kernel.cuh"
+
+namespace ftb {
+
+// Workspace limits, the arguments of init_tbs_gpu
+// (lib/marisa/grimoire/trie/tbs-kernels.cu:599-648).
+struct EngineLimits {
+  uint64_t max_batch = 1;
+  uint64_t max_topk = 1024;
+  uint64_t max_outpos = 64;
+  uint64_t max_out_beams = 8192;
+  uint64_t max_out_tokens = 8192 * 64;
+  uint64_t max_inter_beams = 1024 * 1024;
+  uint64_t radix_topk_threshold = 1024;
+};
+
+// Hard limits of the kernel (shared-memory row staging and result sort).
+constexpr uint64_t kMaxTopk = 8192;
+constexpr uint64_t kMaxBeams = 8192;
+constexpr uint64_t kMaxOutpos = 65535;
+
+class InvalidArgument : public std::runtime_error {
+ public:
+  explicit InvalidArgument(const std::string &m) : std::runtime_error(m) {}
+};
+
+class Engine {
+ public:
+  Engine(std::shared_ptr<DeviceTrie> trie, const EngineLimits &lim);
+  ~Engine();
+  Engine(const Engine &) = delete;
+  Engine &operator=(const Engine &) = delete;
+
+  const EngineLimits &limits() const { return lim_; }
+  void search_host(const ft_request *reqs, uint32_t n, const ft_search_params &prm, ft_result *out);
+  void search_device(const ft_device_batch &b, const ft_search_params &prm, cudaStream_t stream);
+  uint32_t read_status();
+
+ private:
+  struct DevBuf {
+    void *p = nullptr;
+    size_t bytes = 0;
+  };
+  void *dalloc(size_t bytes);
+  void release();
+  void validate_request(const ft_request &r) const;
+  void fill_params(SearchParams &sp, const ft_search_params &prm, uint32_t n_req) const;
+
+  std::shared_ptr<DeviceTrie> trie_;
+  EngineLimits lim_;
+  int device_ = -1;
+  int max_ctas_ = 1;
+  uint32_t n_slots_ = 1;
+  size_t smem_ = 0;
+  std::vector<DevBuf> allocs_;
+  // device workspace
+  SlotView *d_slots_ = nullptr;
+  uint32_t *d_row_id_ = nullptr;
+  float *d_row_lp_ = nullptr;
+  uint32_t *d_row_orig_ = nullptr;
+  uint32_t *d_status_ = nullptr;
+  // staging: [meta | factor | beams | ids | logp] on device and pinned host
+  uint8_t *d_in_ = nullptr;
+  uint8_t *h_in_ = nullptr;
+  size_t in_bytes_ = 0;
+  // outputs: [status | count | phase | lpn | len | tok]
+  uint8_t *d_out_ = nullptr;
+  uint8_t *h_out_ = nullptr;
+  size_t out_bytes_ = 0;
+  // device-path meta/factor staging
+  uint8_t *d_dmeta_ = nullptr;
+  uint8_t *h_dmeta_ = nullptr;
+  size_t dmeta_bytes_ = 0;
+  cudaStream_t stream_ = nullptr;
+  cudaEvent_t dmeta_done_ = nullptr;
+  std::mutex mu_;
+};
+
+}  // namespace ftb

@@ -1,0 +1,71 @@
+# Build recipe for the UNMODIFIED reference FlashTrie (Dakshitha-BA/flash-trie)
+# from its own sources, without running the reference's CMake build.
+#
+# Test infrastructure only: the result is the reference's pybind11 module,
+# renamed to `flashtrie_ref` at compile time so it can sit beside this
+# project's own `flashtrie` module.  It is used to generate golden vectors
+# (tests/golden/make_golden.py) and as the timed CPU baseline
+# (`bench.py --impl reference`).  Nothing in the product links or imports it.
+#
+#   make -f oracle/ref.mk REF=/path/to/reference        (from the repo root)
+#
+# Output: oracle/_ref/flashtrie_ref$(EXT) (git-ignored, travels to the GPU box)
+#
+# Flags follow the reference's CMakeLists.txt:21-27 except -march=native and
+# -mbmi2: the module is built here and run on another host, so it uses the
+# portable popcount path only (select_bit then takes the table path,
+# bit-vector.cc:33-392, which computes the same positions).
+
+REF      ?= /root/reference
+OUT      := oracle/_ref
+OBJ      := $(OUT)/obj
+PYINC    := $(shell python3 -c "import sysconfig;print(sysconfig.get_paths()['include'])")
+PYBIND   := $(shell python3 -c "import pybind11;print(pybind11.get_include())")
+EXT      := $(shell python3 -c "import sysconfig;print(sysconfig.get_config_var('EXT_SUFFIX'))")
+NVCC     ?= nvcc
+CXX      := /usr/bin/g++
+ARCH     := -gencode arch=compute_100a,code=sm_100a
+INCS     := -I$(REF)/include -I$(REF)/lib -I/usr/local/cuda/include
+DEFS     := -DMARISA_USE_POPCNT -DNDEBUG
+HOSTFL   := -O3 -std=c++17 -fPIC -fopenmp -mpopcnt -w
+CUFLAGS  := -O3 -std=c++17 -rdc=true --expt-relaxed-constexpr -lineinfo $(ARCH) \
+            -ccbin $(CXX) -Xcompiler -fPIC,-fopenmp,-mpopcnt,-O3 -w $(INCS) $(DEFS)
+CXXFLAGS := $(HOSTFL) $(INCS) $(DEFS)
+
+CU_SRCS  := lib/marisa/grimoire/trie/louds-trie.cc lib/marisa/grimoire/trie/tail.cc \
+            lib/marisa/grimoire/vector/bit-vector.cc
+CXX_SRCS := lib/marisa/keyset.cc lib/marisa/agent.cc lib/marisa/trie.cc \
+            lib/marisa/grimoire/io/mapper.cc lib/marisa/grimoire/io/reader.cc \
+            lib/marisa/grimoire/io/writer.cc
+CU_OBJS  := $(patsubst %.cc,$(OBJ)/%.o,$(CU_SRCS))
+CXX_OBJS := $(patsubst %.cc,$(OBJ)/%.o,$(CXX_SRCS))
+BIND_OBJ := $(OBJ)/tools/bindings.o
+DLINK    := $(OBJ)/dlink.o
+MODULE   := $(OUT)/flashtrie_ref$(EXT)
+
+all: $(MODULE)
+
+$(CU_OBJS): $(OBJ)/%.o: $(REF)/%.cc
+	@mkdir -p $(dir $@)
+	$(NVCC) $(CUFLAGS) -x cu -c $< -o $@
+
+$(CXX_OBJS): $(OBJ)/%.o: $(REF)/%.cc
+	@mkdir -p $(dir $@)
+	$(CXX) $(CXXFLAGS) -c $< -o $@
+
+# The module name is a token in bindings.cpp (PYBIND11_MODULE(flashtrie, m));
+# -Dflashtrie=flashtrie_ref renames it without touching the source.
+$(BIND_OBJ): $(REF)/tools/bindings.cpp
+	@mkdir -p $(dir $@)
+	$(CXX) $(CXXFLAGS) -Dflashtrie=flashtrie_ref -I$(REF)/tools -I$(PYINC) -I$(PYBIND) -c $< -o $@
+
+$(DLINK): $(CU_OBJS)
+	$(NVCC) $(ARCH) -Xcompiler -fPIC -dlink $^ -o $@
+
+$(MODULE): $(CU_OBJS) $(CXX_OBJS) $(BIND_OBJ) $(DLINK)
+	$(CXX) -shared -fopenmp -o $@ $^ -L/usr/local/cuda/lib64 -lcudart -Wl,-rpath,/usr/local/cuda/lib64
+
+clean:
+	rm -rf $(OUT)
+
+.PHONY: all clean

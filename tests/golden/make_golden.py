@@ -1,0 +1,152 @@
+"""Generates the golden fixtures in tests/golden/ from the UNMODIFIED reference.
+
+Run in a container that has the reference sources and the module built by
+oracle/ref.mk (`make -f oracle/ref.mk`):
+
+    python tests/golden/make_golden.py
+
+Fixtures (JSON):
+  format.json   for seeded key sets: sha256 and size of the file the reference
+                `Trie.build(...).save()` writes (the engine's builder must write
+                the same bytes), plus num_keys/num_nodes/total_size/io_size.
+  search_c1.json
+                config-1 trie (100k keys) and seeded requests: the reference
+                CPU `tbs(use_gpu=False)` output for each, whether that output
+                holds beams that are not keys (the reference CPU link-node bug),
+                and a sha256 of the generated inputs so generator drift fails
+                loudly instead of comparing different inputs.
+  search_hand.json
+                hand-built tries and requests covering links, internal link
+                nodes, terminal link nodes, thresholds, ties, duplicate ids,
+                unsorted rows and zero-width beams.
+The reference never runs on the GPU box; only these files travel.
+"""
+import hashlib
+import json
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, REPO)
+sys.path.insert(0, os.path.join(REPO, "oracle", "_ref"))
+os.environ.setdefault("MARISA_MANAGED_ALLOC", "0")
+
+import workload as W  # noqa: E402
+
+THR = (W.TOKEN_LOGP_THRESHOLD, W.SENT_LOGP_THRESHOLD, W.LENGTH_NORM)
+
+
+def sha(*arrays):
+    h = hashlib.sha256()
+    for a in arrays:
+        h.update(np.ascontiguousarray(a).tobytes())
+    return h.hexdigest()
+
+
+def file_sha(path):
+    with open(path, "rb") as f:
+        return hashlib.sha256(f.read()).hexdigest()
+
+
+def format_cases():
+    rng = np.random.default_rng(7)
+    cases = []
+    for name, n, V, lo, hi in [("tiny-random", 40, 6, 1, 4), ("small-random", 3000, 40, 1, 7),
+                                ("mid-random", 20000, 70000, 2, 9), ("wide-labels", 5000, 2**31 - 1, 1, 6)]:
+        rows = [rng.integers(0, V, size=int(rng.integers(lo, hi + 1))).tolist() for _ in range(n)]
+        cases.append((name, rows))
+    tok, off = W.gen_keys(100_000, 32_000, 2, 8, 1.1, seed=1)
+    cases.append(("config1-keys", W.key_rows(tok, off)))
+    cases.append(("empty", []))
+    cases.append(("empty-key", [[]]))
+    cases.append(("duplicates", [[5], [5], [5, 6], [5, 6], [9, 9, 9]]))
+    return cases
+
+
+def main():
+    import flashtrie_ref as ref
+    from oracle.oracle import OracleTrie
+
+    out = {"generator": "tests/golden/make_golden.py", "cases": []}
+    for name, rows in format_cases():
+        t = ref.Trie()
+        t.build(token_rows=rows)
+        path = "/tmp/golden_%s.bin" % name
+        t.save(path)
+        out["cases"].append({"name": name, "sha256": file_sha(path), "bytes": os.path.getsize(path),
+                             "num_keys": t.num_keys(), "num_nodes": t.num_nodes(), "total_size": t.total_size()})
+    with open(os.path.join(HERE, "format.json"), "w") as f:
+        json.dump(out, f, indent=1)
+
+    # ---- config 1 search goldens
+    cfg = W.CONFIGS[1]
+    tok, off = W.gen_keys(cfg["keys"], cfg["vocab"], cfg["len_lo"], cfg["len_hi"], cfg["zipf"], seed=1)
+    t = ref.Trie()
+    t.build(token_rows=W.key_rows(tok, off))
+    path = "/tmp/golden_c1.bin"
+    t.save(path)
+    orc = OracleTrie(path)
+    reqs = []
+    n_req = 160
+    beams, ids, lp = W.gen_requests(1, tok, off, n_req)
+    for r in range(n_req):
+        ee = r >= 120  # the last 40 use early exit
+        sent, lpn, _ = ref.tbs(t, beams[r].tolist(), ids[r].tolist(), lp[r].tolist(), *THR, ee, False)
+        invalid = [i for i, s in enumerate(sent) if not orc.lookup(s)]
+        reqs.append({"index": r, "seed": 1000 + r, "inputs_sha256": sha(beams[r], ids[r], lp[r]),
+                     "early_exit": ee, "ref_sent": sent, "ref_lpn": lpn, "ref_invalid": invalid})
+    with open(os.path.join(HERE, "search_c1.json"), "w") as f:
+        json.dump({"config": 1, "key_seed": 1, "keys_sha256": sha(tok, off), "trie_sha256": file_sha(path),
+                   "thresholds": THR, "requests": reqs}, f)
+
+    # ---- hand-built tries
+    hand = []
+    keysets = {
+        # links, an internal link node ([20,21,22] is a link node with a child),
+        # a terminal internal link node, a single-label key
+        "links": [[1, 2, 3, 4], [1, 2, 3, 5], [20, 21, 22], [20, 21, 22, 23], [7]],
+        "deep": [[1, 2, 3, 4, 5, 6, 7, 8], [1, 2, 3, 4, 5, 6, 7, 9], [1, 2, 9], [1, 2], [1], [3, 3, 3, 3]],
+        "fan": [[i, j] for i in range(1, 6) for j in range(0, 40, 3)] + [[100 + i] for i in range(50)],
+    }
+    rng = np.random.default_rng(11)
+    for name, keys in keysets.items():
+        t = ref.Trie()
+        t.build(token_rows=keys)
+        for q in range(24):
+            L = int(rng.integers(1, 9))
+            K = int(rng.integers(1, 12))
+            vocab = sorted({k for key in keys for k in key} | {0, 99, 1000})
+            rows_i, rows_l = [], []
+            for _ in range(L):
+                row = rng.choice(vocab, size=K, replace=bool(q % 5 == 4)).tolist()
+                if q % 3 != 2:
+                    row = sorted(row)
+                rows_i.append([int(x) for x in row])
+                # coarse values so that exact ties occur
+                rows_l.append([float(np.float32(-0.5 * int(rng.integers(0, 6)))) for _ in range(K)])
+            B = int(rng.integers(1, 6))
+            beams_q = [B] * L
+            # (A zero width before the last position crashes the reference CPU
+            # path: Candidates::push reads top() of an empty heap,
+            # candidates.h:223.  Zero widths are covered by the oracle tests.)
+            tt, st = (-10.0, -40.0) if q % 4 else (-1.6, -3.1)
+            ln = [0.0, 1.0, 5.0][q % 3]
+            ee = bool(q % 8 == 7)
+            sent, lpn, _ = ref.tbs(t, beams_q, rows_i, rows_l, tt, st, ln, ee, False)
+            # The oracle has its own trie loader; check on the same file bytes.
+            t.save("/tmp/golden_hand.bin")
+            orc = OracleTrie("/tmp/golden_hand.bin")
+            invalid = [i for i, s in enumerate(sent) if not orc.lookup(s)]
+            hand.append({"trie": name, "beams": beams_q, "topk_id": rows_i, "topk_logp": rows_l,
+                         "token_logp_threshold": tt, "sents_logp_threshold": st, "length_norm": ln,
+                         "early_exit": ee, "ref_sent": sent, "ref_lpn": lpn, "ref_invalid": invalid})
+    with open(os.path.join(HERE, "search_hand.json"), "w") as f:
+        json.dump({"keysets": keysets, "requests": hand}, f)
+    print("wrote", os.listdir(HERE))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,41 @@
+"""The C-ABI library loads and exports every entry point include/*.h declares
+(no device calls: this runs without a GPU)."""
+import ctypes
+import glob
+import os
+import re
+
+from helpers import REPO
+
+
+def declared_symbols():
+    names = set()
+    for h in glob.glob(os.path.join(REPO, "include", "*.h")):
+        src = open(h).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        for m in re.finditer(r"^\s*(?:const\s+)?[A-Za-z_][A-Za-z0-9_]*\s*\*?\s*(ft_[A-Za-z0-9_]+)\s*\(", src, re.M):
+            names.add(m.group(1))
+    return names
+
+
+def test_library_exports_declared_symbols(built):
+    lib = ctypes.CDLL(os.path.join(REPO, "flash-trie_b200", "libftcore.so"))
+    names = declared_symbols()
+    assert len(names) >= 14
+    missing = [n for n in sorted(names) if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_host_entry_points_without_gpu(built, tmp_path):
+    lib = ctypes.CDLL(os.path.join(REPO, "flash-trie_b200", "libftcore.so"))
+    lib.ft_last_error.restype = ctypes.c_char_p
+    h = ctypes.c_void_p()
+    assert lib.ft_trie_create(ctypes.byref(h)) == 0
+    toks = (ctypes.c_uint32 * 5)(1, 2, 3, 1, 2)
+    offs = (ctypes.c_uint64 * 3)(0, 3, 5)
+    assert lib.ft_trie_build(h, toks, offs, ctypes.c_uint64(2)) == 0
+    p = str(tmp_path / "t.bin").encode()
+    assert lib.ft_trie_save(h, p) == 0
+    assert lib.ft_trie_load(h, b"/nonexistent/trie.bin") == -9  # FT_ERR_IO
+    assert b"IO_ERROR" in lib.ft_last_error()
+    lib.ft_trie_destroy(h)
