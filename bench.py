@@ -330,8 +330,24 @@ def run_b200(args, cfg):
     st = ctypes.c_uint32()
     assert lib.ft_trie_device_status(handle, ctypes.byref(st)) == 0 and st.value == 0, "device status %d" % st.value
 
+    # Clocks are sampled by nvidia-smi (100 ms period) from before until after
+    # the timed region; a short sustained loop of the same step on each side
+    # keeps the GPU under load for the sampler when the timed region itself
+    # is shorter than a sampling period.
     clocks = Clocks(local)
     clocks.start()
+
+    def sustained(seconds):
+        t_end = time.time() + seconds
+        k = 0
+        while time.time() < t_end:
+            with torch.cuda.stream(stream):
+                for _ in range(16):
+                    launch(k)
+                    k += 1
+            stream.synchronize()
+
+    sustained(0.6)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     barrier()
     torch.cuda.synchronize()
@@ -347,6 +363,7 @@ def run_b200(args, cfg):
     barrier()
     elapsed_ms = t_start.elapsed_time(t_end)
     step_ms = np.array([a.elapsed_time(b) for a, b in ev])
+    sustained(0.4)
     clk = clocks.stop()
     assert lib.ft_trie_device_status(handle, ctypes.byref(st)) == 0 and st.value == 0, "device status %d" % st.value
 

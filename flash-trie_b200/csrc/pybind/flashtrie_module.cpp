@@ -303,12 +303,11 @@ py::tuple bs_tbs_gpu(PyTrie &trie, size_t batch_size, py::object batch_beams, py
     lp_arr = py::array_t<float, py::array::c_style | py::array::forcecast>::ensure(batch_topk_logp);
   }
   for (size_t i = 0; i < batch_size; ++i) {
-    py::handle b = batch_beams[py::int_(i)];
-    if (arr3) {
-      convert_request(b, ids_arr[py::int_(i)], lp_arr[py::int_(i)], reqs[i]);
-    } else {
-      convert_request(b, batch_topk_id[py::int_(i)], batch_topk_logp[py::int_(i)], reqs[i]);
-    }
+    // Owning references: indexing a numpy array creates a new view object.
+    py::object b = batch_beams[py::int_(i)];
+    py::object ri = arr3 ? py::object(ids_arr[py::int_(i)]) : py::object(batch_topk_id[py::int_(i)]);
+    py::object rl = arr3 ? py::object(lp_arr[py::int_(i)]) : py::object(batch_topk_logp[py::int_(i)]);
+    convert_request(b, ri, rl, reqs[i]);
     if (reqs[i].L == 0) throw py::value_error("bs_tbs_gpu: beams must not be empty");
   }
   const auto start = std::chrono::high_resolution_clock::now();
