@@ -57,7 +57,7 @@ def parse():
     ap.add_argument("--beam", type=int, default=0, help="override the config's beam width")
     ap.add_argument("--keys", type=int, default=0, help="override the config's key count (smoke runs only)")
     ap.add_argument("--requests", type=int, default=64, help="distinct requests cycled through")
-    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference", "reference-gpu"])
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of reference CPU work to time")
     ap.add_argument("--trie-dir", default="/tmp")
     return ap.parse_args()
@@ -275,6 +275,56 @@ def run_reference(args, cfg):
     print(json.dumps(line))
 
 
+def run_reference_gpu(args, cfg):
+    """The reference's own GPU kernel (its sources compiled unmodified for
+    sm_100a by oracle/ref.mk), one request per call (batch 1, one cooperative
+    grid at a time), timed the way the reference reports it: the `ms` its
+    `tbs` binding returns (tools/bindings.cpp:54-64).  Not a driver arm; used
+    to compare the engine with the reference kernel on the same B200."""
+    rank, world, local = dist_env()
+    if rank != 0:
+        return
+    # The reference kernel reads the trie through managed memory
+    # (vector.h:222-235, 484-492); host-malloc'd arrays would be host pointers.
+    os.environ["MARISA_MANAGED_ALLOC"] = "1"
+    sys.path.insert(0, os.path.join(REPO, "oracle", "_ref"))
+    import flashtrie_ref as ref
+    import torch
+    from oracle.oracle import OracleTrie
+    path, tok, off, beams, ids, lp, _ = load_workload(args, cfg, 0, 1, "cuda", lambda: None)
+    B, L, K = cfg["beam"], cfg["L"], cfg["K"]
+    t = ref.Trie()
+    t.load(path)
+    # Buffers sized well above one step's worst case (B*K candidates) and the
+    # history (max_num_inter_beams) above 1 + L*B saved beams.
+    t.init_tbs_gpu(1, max_num_topk=K, max_num_outpos=L, max_num_out_beams=4 * B,
+                   max_num_out_tokens=4 * B * L, max_num_inter_beams=4 * B * L + 64)
+    o = OracleTrie(path)
+    args_t = (W.TOKEN_LOGP_THRESHOLD, W.SENT_LOGP_THRESHOLD, W.LENGTH_NORM, cfg["early_exit"])
+    lists = [(beams[i].tolist(), ids[i].tolist(), lp[i].tolist()) for i in range(len(beams))]
+    for i in range(min(args.warmup, len(lists))):
+        ref.tbs(t, *lists[i], *args_t, True)
+    torch.cuda.synchronize()
+    ms, same_sets = [], 0
+    for s in range(args.steps):
+        b_, i_, l_ = lists[s % len(lists)]
+        sent, lpn, m = ref.tbs(t, b_, i_, l_, *args_t, True)
+        ms.append(m)
+        if s < len(lists):
+            o_sent, o_lpn = o.tbs(beams[s], ids[s], lp[s], *args_t)
+            a = sorted(zip(map(tuple, sent), [round(x, 9) for x in lpn]))
+            b = sorted(zip(map(tuple, o_sent), [round(x, 9) for x in o_lpn]))
+            same_sets += int(a == b)
+    ms = np.array(ms)
+    print(json.dumps({"impl": "reference-gpu", "metric": METRIC, "value": 1e3 / ms.mean(), "unit": UNIT,
+                      "latency_ms": {"mean": float(ms.mean()), "p50": float(np.percentile(ms, 50)),
+                                     "p99": float(np.percentile(ms, 99)),
+                                     "per": "request, the reference binding's own ms (2-decimal truncation)"},
+                      "steps": args.steps, "config": {"workload": "config%d" % args.config, "keys": cfg["keys"],
+                                                      "K": K, "L": L, "beam": B, "batch": 1},
+                      "result_sets_equal_to_oracle": "%d of %d" % (same_sets, min(args.steps, len(lists)))}))
+
+
 def run_b200(args, cfg):
     import torch
     import flashtrie
@@ -374,12 +424,14 @@ def run_b200(args, cfg):
         flashtrie.bs_tbs_gpu(trie, nb, beams[i:i + nb], ids[i:i + nb], lp[i:i + nb], W.TOKEN_LOGP_THRESHOLD,
                              W.SENT_LOGP_THRESHOLD, W.LENGTH_NORM, cfg["early_exit"])
     d2h = 0
+    binding_ms = []
     t0 = time.perf_counter()
     for s in range(e2e_steps):
         i = (s % n_slices) * nb
-        sents, lpns, _, _ = flashtrie.bs_tbs_gpu(trie, nb, beams[i:i + nb], ids[i:i + nb], lp[i:i + nb],
-                                                 W.TOKEN_LOGP_THRESHOLD, W.SENT_LOGP_THRESHOLD, W.LENGTH_NORM,
-                                                 cfg["early_exit"])
+        sents, lpns, bms, _ = flashtrie.bs_tbs_gpu(trie, nb, beams[i:i + nb], ids[i:i + nb], lp[i:i + nb],
+                                                   W.TOKEN_LOGP_THRESHOLD, W.SENT_LOGP_THRESHOLD, W.LENGTH_NORM,
+                                                   cfg["early_exit"])
+        binding_ms.append(bms)
         d2h += 16 + nb * (4 + 40) + nb * B * (8 + 4 + 4 * L)
     e2e_s = time.perf_counter() - t0
     h2d_step = nb * (L * 4 + L * K * 8 + 24) + 8 * (L + 1)
@@ -419,7 +471,8 @@ def run_b200(args, cfg):
                            "p99": float(np.percentile(step_ms, 99)), "per": "step (batch of %d)" % nb},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(h2d_step),
                     "d2h_bytes_per_step": int(d2h / max(e2e_steps, 1)),
-                    "path": "flashtrie.bs_tbs_gpu (numpy host buffers)"},
+                    "path": "flashtrie.bs_tbs_gpu (numpy host buffers)",
+                    "binding_ms": {"mean": float(np.mean(binding_ms)), "p99": float(np.percentile(binding_ms, 99))}},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": None, "peak_source": peak_kind,
                          "bytes_alg_per_launch": bytes_per_launch},
@@ -441,6 +494,8 @@ def main():
     cfg = workload_cfg(args)
     if args.impl == "reference":
         run_reference(args, cfg)
+    elif args.impl == "reference-gpu":
+        run_reference_gpu(args, cfg)
     else:
         run_b200(args, cfg)
 

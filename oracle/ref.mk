@@ -11,10 +11,11 @@
 #
 # Output: oracle/_ref/flashtrie_ref$(EXT) (git-ignored, travels to the GPU box)
 #
-# Flags follow the reference's CMakeLists.txt:21-27 except -march=native and
-# -mbmi2: the module is built here and run on another host, so it uses the
-# portable popcount path only (select_bit then takes the table path,
-# bit-vector.cc:33-392, which computes the same positions).
+# Flags follow the reference's CMakeLists.txt:21-27 (MARISA_USE_POPCNT,
+# MARISA_USE_BMI2, -mpopcnt -mbmi2) except -march=native, since the module is
+# built here and run on another x86-64 host.  MARISA_USE_BMI2 is required for
+# the GPU path: without it the device-side select0 would call the host-only
+# table version of select_bit (bit-vector.cc:18-31 vs :33-392).
 
 REF      ?= /root/reference
 OUT      := oracle/_ref
@@ -26,10 +27,10 @@ NVCC     ?= nvcc
 CXX      := /usr/bin/g++
 ARCH     := -gencode arch=compute_100a,code=sm_100a
 INCS     := -I$(REF)/include -I$(REF)/lib -I/usr/local/cuda/include
-DEFS     := -DMARISA_USE_POPCNT -DNDEBUG
-HOSTFL   := -O3 -std=c++17 -fPIC -fopenmp -mpopcnt -w
+DEFS     := -DMARISA_USE_POPCNT -DMARISA_USE_BMI2 -DNDEBUG
+HOSTFL   := -O3 -std=c++17 -fPIC -fopenmp -mpopcnt -mbmi2 -w
 CUFLAGS  := -O3 -std=c++17 -rdc=true --expt-relaxed-constexpr -lineinfo $(ARCH) \
-            -ccbin $(CXX) -Xcompiler -fPIC,-fopenmp,-mpopcnt,-O3 -w $(INCS) $(DEFS)
+            -ccbin $(CXX) -Xcompiler -fPIC,-fopenmp,-mpopcnt,-mbmi2,-O3,-w $(INCS) $(DEFS)
 CXXFLAGS := $(HOSTFL) $(INCS) $(DEFS)
 
 CU_SRCS  := lib/marisa/grimoire/trie/louds-trie.cc lib/marisa/grimoire/trie/tail.cc \
