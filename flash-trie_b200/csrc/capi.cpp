@@ -27,6 +27,17 @@ struct ft_trie {
   std::mutex mu;
 };
 
+namespace ftb {
+// Device image of a trie handle (nullptr before init_tbs_gpu); used by the
+// no-allocation entry point in device/noalloc.cu.
+std::shared_ptr<DeviceTrie> device_trie_of(ft_trie *t) {
+  if (!t) return nullptr;
+  std::lock_guard<std::mutex> lock(t->mu);
+  return t->dev;
+}
+void set_last_error(const std::string &m);
+}  // namespace ftb
+
 namespace {
 
 thread_local std::string g_last_error;
@@ -87,6 +98,8 @@ void drop_device(ft_trie *t) {
 }
 
 }  // namespace
+
+void ftb::set_last_error(const std::string &m) { g_last_error = m; }
 
 extern "C" {
 

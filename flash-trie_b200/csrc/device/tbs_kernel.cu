@@ -752,6 +752,22 @@ int configure_search_kernel(size_t smem_bytes) {
   return std::max(per_sm, 1) * sms;
 }
 
+int ensure_search_smem(size_t search_smem, size_t prep_smem) {
+  cudaFuncAttributes a;
+  CUDA_TRY(cudaFuncGetAttributes(&a, tbs_search_kernel));
+  if ((size_t)a.maxDynamicSharedSizeBytes < search_smem)
+    CUDA_TRY(cudaFuncSetAttribute(tbs_search_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)search_smem));
+  CUDA_TRY(cudaFuncGetAttributes(&a, row_prep_kernel));
+  if ((size_t)a.maxDynamicSharedSizeBytes < prep_smem)
+    CUDA_TRY(cudaFuncSetAttribute(row_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem));
+  int per_sm = 0;
+  CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tbs_search_kernel, kSearchThreads, search_smem));
+  int dev = 0, sms = 0;
+  CUDA_TRY(cudaGetDevice(&dev));
+  CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  return std::max(per_sm, 1) * sms;
+}
+
 void launch_search(const SearchParams &p, uint32_t max_K, uint32_t max_L, size_t smem_bytes, int grid,
                    cudaStream_t stream) {
   if (p.n_req == 0) return;

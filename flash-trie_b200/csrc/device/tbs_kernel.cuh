@@ -117,4 +117,9 @@ void launch_search(const SearchParams &p, uint32_t max_K, uint32_t max_L, size_t
 // Configures kernel attributes once per device; returns max resident search CTAs.
 int configure_search_kernel(size_t smem_bytes);
 
+// Raises (never lowers) the dynamic shared-memory limits of the search and
+// row-prep kernels on the current device; returns max resident search CTAs
+// for `search_smem`.
+int ensure_search_smem(size_t search_smem, size_t prep_smem);
+
 }  // namespace ftb

@@ -162,6 +162,24 @@ int ft_tbs_batch_device(ft_trie *trie, const ft_device_batch *batch,
  * the first bounds check that failed inside the kernel. */
 int ft_trie_device_status(ft_trie *trie, uint32_t *status);
 
+/*
+ * No counterpart in the reference.  The same search as ft_tbs_batch_device,
+ * for callers that cannot allocate device memory while they search: code whose
+ * host framework owns every device allocation, or request threads that must
+ * not stall on cudaMalloc/cudaFree.  It allocates nothing; its scratch is a
+ * fixed 8 MiB array in the library, which every GPU that loads the library
+ * keeps until exit.  The trie must already be on the device
+ * (ft_trie_init_tbs_gpu); the caller passes device inputs and outputs as for
+ * ft_tbs_batch_device, with every beam width at most out_capacity.  Batches
+ * whose scratch would exceed 8 MiB are rejected with FT_ERR_INVALID_ARG.
+ * The first call on a device looks up the array's address; make it before any
+ * stream capture.  Calls are serialised per device and return after the
+ * stream has finished the search; all calls share the array, so searches
+ * whose GPU work overlapped would race.
+ */
+int ft_tbs_batch_device_noalloc(ft_trie *trie, const ft_device_batch *batch,
+                                const ft_search_params *params, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
