@@ -425,13 +425,15 @@ def run_b200(args, cfg):
                              W.SENT_LOGP_THRESHOLD, W.LENGTH_NORM, cfg["early_exit"])
     d2h = 0
     binding_ms = []
+    phase_sum = np.zeros(5)
     t0 = time.perf_counter()
     for s in range(e2e_steps):
         i = (s % n_slices) * nb
-        sents, lpns, bms, _ = flashtrie.bs_tbs_gpu(trie, nb, beams[i:i + nb], ids[i:i + nb], lp[i:i + nb],
-                                                   W.TOKEN_LOGP_THRESHOLD, W.SENT_LOGP_THRESHOLD, W.LENGTH_NORM,
-                                                   cfg["early_exit"])
+        sents, lpns, bms, phases = flashtrie.bs_tbs_gpu(trie, nb, beams[i:i + nb], ids[i:i + nb], lp[i:i + nb],
+                                                        W.TOKEN_LOGP_THRESHOLD, W.SENT_LOGP_THRESHOLD, W.LENGTH_NORM,
+                                                        cfg["early_exit"])
         binding_ms.append(bms)
+        phase_sum += np.asarray(phases, dtype=np.float64).sum(axis=0)
         d2h += 16 + nb * (4 + 40) + nb * B * (8 + 4 + 4 * L)
     e2e_s = time.perf_counter() - t0
     h2d_step = nb * (L * 4 + L * K * 8 + 24) + 8 * (L + 1)
@@ -479,6 +481,8 @@ def run_b200(args, cfg):
             "cpu_baseline": ({"value": cpu_qps, "unit": UNIT, "cores": 1, "kind": "reference",
                               "sample": "%d requests of config %d, %.1f s, reference tbs(use_gpu=False), 1 core"
                                         % (cpu_n, args.config, cpu_wall)} if cpu_qps else None),
+            "phase_ms_per_request": dict(zip(["expansion", "validation(fused)", "selection", "overhead", "kernel"],
+                                              (phase_sum / max(e2e_steps * nb, 1)).round(5).tolist())),
             "clocks": clk,
             "gpu_launches": 2 * args.steps,
             "setup_s": {"trie_build": build_s, "init_tbs_gpu": init_s},

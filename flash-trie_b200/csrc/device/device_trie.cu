@@ -9,6 +9,8 @@
 
 namespace ftb {
 
+void build_hash_index(HostDeviceImage &out, int num_threads);
+
 void derive_device_image(const LoudsLevel &lv, HostDeviceImage &out, int num_threads) {
   if (lv.next) fail(ErrorKind::kState, "MARISA_STATE_ERROR: the GPU search needs a single-trie dictionary (num_tries == 1)");
   if (lv.node_order() != kLabelOrder)
@@ -73,8 +75,13 @@ void derive_device_image(const LoudsLevel &lv, HostDeviceImage &out, int num_thr
         // The kernel reads tail[off] and tail[off + 1] (text) or tail[off]
         // and the end bit at off (binary); the terminator / end bit that
         // closes the tail bounds every later step of the walk.
-        if (out.binary_tail ? (off >= T) : (off + 1 >= T)) bad = true;
-        if (off < T) out.first_label[n] = lv.tail[off];
+        if (out.binary_tail ? (off >= T) : (off + 1 >= T)) {
+          bad = true;
+        } else {
+          out.first_label[n] = lv.tail[off];
+          const bool ends1 = out.binary_tail ? lv.tail_end_flags.get(off) : lv.tail[off + 1] == kTailTerminal;
+          if (ends1) f |= kNodeLinkEnds1;
+        }
         out.link_off[n] = (uint32_t)off;
       } else {
         out.first_label[n] = lv.label(n);
@@ -99,6 +106,47 @@ void derive_device_image(const LoudsLevel &lv, HostDeviceImage &out, int num_thr
   if (unsorted)
     fail(ErrorKind::kFormat,
          "MARISA_FORMAT_ERROR: children are not in ascending label order (the GPU search binary-searches them)");
+  build_hash_index(out, num_threads);
+}
+
+void build_hash_index(HostDeviceImage &out, int num_threads) {
+  const uint64_t N = out.num_nodes;
+  std::vector<uint32_t> heavy;
+  for (uint64_t n = 0; n < N; ++n) {
+    const uint32_t d = out.child_begin[n + 1] - out.child_begin[n];
+    if (d >= kHashMinDegree && !(out.flags[n] & kNodeLink)) heavy.push_back((uint32_t)n);
+  }
+  std::vector<uint64_t> base(heavy.size());
+  std::vector<uint32_t> lgs(heavy.size());
+  uint64_t total = 0;
+  size_t used = 0;
+  for (; used < heavy.size(); ++used) {
+    const uint32_t n = heavy[used];
+    const uint64_t d = out.child_begin[n + 1] - out.child_begin[n];
+    uint32_t lg = 1;
+    while ((1ull << lg) < 2 * d) ++lg;
+    if (lg > 31 || total + (1ull << lg) >= 0xFFFFFFFFull) break;  // offsets must fit link_off
+    base[used] = total;
+    lgs[used] = lg;
+    total += 1ull << lg;
+  }
+  out.hash.assign(2 * total, 0);
+#pragma omp parallel for schedule(dynamic, 64) num_threads(num_threads)
+  for (int64_t i = 0; i < (int64_t)used; ++i) {
+    const uint32_t n = heavy[i];
+    const uint32_t lg = lgs[i];
+    const uint64_t mask = (1ull << lg) - 1;
+    uint32_t *tab = out.hash.data() + 2 * base[i];
+    for (uint32_t c = out.child_begin[n]; c < out.child_begin[n + 1]; ++c) {
+      const uint32_t lab = out.first_label[c];
+      uint64_t h = hash_slot(lab, lg);
+      while (tab[2 * h + 1] != 0) h = (h + 1) & mask;
+      tab[2 * h] = lab;
+      tab[2 * h + 1] = c;
+    }
+    out.link_off[n] = (uint32_t)base[i];
+    out.flags[n] = (uint8_t)(out.flags[n] | kNodeHashed | (lg << 3));
+  }
 }
 
 DeviceTrie::~DeviceTrie() { release(); }
@@ -114,11 +162,14 @@ void DeviceTrie::release() {
     cudaFree(flags);
     cudaFree(tail);
     cudaFree(tail_end);
+    cudaFree(hash);
     if (prev >= 0) cudaSetDevice(prev);
   }
   child_begin = first_label = link_off = tail = nullptr;
   flags = nullptr;
   tail_end = nullptr;
+  hash = nullptr;
+  hash_slots = 0;
   device = -1;
   bytes = 0;
 }
@@ -149,6 +200,8 @@ void DeviceTrie::upload(const LoudsLevel &lv, int num_threads) {
     flags = upload_array(img.flags.data(), img.flags.size(), bytes);
     tail = upload_array(lv.tail.data(), lv.tail.size(), bytes);
     if (binary_tail) tail_end = upload_array(lv.tail_end_flags.units.data(), lv.tail_end_flags.units.size(), bytes);
+    hash = upload_array(img.hash.data(), img.hash.size(), bytes);
+    hash_slots = img.hash.size() / 2;
   } catch (...) {
     release();
     throw;

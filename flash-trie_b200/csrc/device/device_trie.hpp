@@ -13,9 +13,18 @@
 //   first_label[n]  u32: the label of a plain child, or the first tail token
 //                   of a link child, so a child range is one sorted u32 run.
 //   link_off[n]     u32: tail offset of a link node's string (0 otherwise).
-//   flags[n]        u8: bit0 terminal, bit1 link.
+//   flags[n]        u8: bit0 terminal, bit1 link; bit2 on a link node: its
+//                   string ends after the first token (the child that consumes
+//                   it cannot continue); bit2 on a plain node: it has a hash
+//                   table (bits 3-7: log2 of the table size).
 //   tail            u32 cells as stored in the file (0xFFFFFFFF terminates a
 //                   string in a text tail); tail_end: end bits of a binary tail.
+//   hash            per-node open-addressing tables for plain (non-link) nodes
+//                   with at least kHashMinDegree children: slots {label, child}
+//                   (child 0 = empty), 2^lg slots at load <= 1/2, located by
+//                   link_off[n] (unused for plain nodes otherwise) with lg in
+//                   flags[n] >> 3.  A proposal then costs one probe instead of a
+//                   log2(fan-out) binary search.
 #pragma once
 
 #include <cstdint>
@@ -27,6 +36,12 @@ namespace ftb {
 
 constexpr uint8_t kNodeTerminal = 1;
 constexpr uint8_t kNodeLink = 2;
+constexpr uint8_t kNodeHashed = 4;      // plain nodes
+constexpr uint8_t kNodeLinkEnds1 = 4;   // link nodes
+constexpr uint32_t kHashMinDegree = 64;
+
+// Slot of a child in its parent's hash table.
+inline uint32_t hash_slot(uint32_t label, uint32_t lg) { return (label * 2654435761u) >> (32 - lg); }
 
 struct HostDeviceImage {
   uint64_t num_nodes = 0;
@@ -34,6 +49,7 @@ struct HostDeviceImage {
   std::vector<uint32_t> first_label;
   std::vector<uint32_t> link_off;
   std::vector<uint8_t> flags;
+  std::vector<uint32_t> hash;  // pairs: label, child
   bool binary_tail = false;
 };
 
@@ -53,6 +69,8 @@ struct DeviceTrie {
   uint8_t *flags = nullptr;
   uint32_t *tail = nullptr;
   uint64_t *tail_end = nullptr;
+  uint32_t *hash = nullptr;
+  uint64_t hash_slots = 0;
   uint64_t bytes = 0;
 
   DeviceTrie() = default;

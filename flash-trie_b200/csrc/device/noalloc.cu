@@ -56,7 +56,7 @@ inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 // Byte offsets of the scratch regions for one call.
 struct Layout {
   size_t status, meta, factor, slots, rows_id, rows_lp, rows_orig, slot0, slot_bytes;
-  size_t cand, pool, pool_tmp, beams0, beams1, hist;  // within a slot
+  size_t hits, cand, pool, pool_tmp, beams0, beams1, hist;  // within a slot
   size_t total;
 };
 
@@ -79,6 +79,8 @@ Layout plan(uint32_t n, uint32_t L, uint32_t K, uint32_t B, uint32_t n_slots) {
   a.rows_orig = o;
   o = align256(o + rows);
   size_t s = 0;
+  a.hits = s;
+  s = align256(s + sizeof(ftb::Hit) * (size_t)B * K);
   a.cand = s;
   s = align256(s + sizeof(ftb::Cand) * (size_t)B * K);
   a.pool = s;
@@ -115,6 +117,7 @@ __global__ void noalloc_setup_kernel(Layout a, uint32_t n, uint32_t L, uint32_t 
   for (uint32_t s = threadIdx.x; s < n_slots; s += blockDim.x) {
     unsigned char *sb = base + a.slot0 + (size_t)s * a.slot_bytes;
     ftb::SlotView v;
+    v.hits = reinterpret_cast<ftb::Hit *>(sb + a.hits);
     v.next = reinterpret_cast<ftb::Cand *>(sb + a.cand);
     v.pool = reinterpret_cast<ftb::Cand *>(sb + a.pool);
     v.pool_tmp = reinterpret_cast<ftb::Cand *>(sb + a.pool_tmp);
@@ -194,14 +197,7 @@ extern "C" int ft_tbs_batch_device_noalloc(ft_trie *trie, const ft_device_batch 
 
     ftb::SearchParams sp;
     std::memset(&sp, 0, sizeof(sp));
-    sp.trie.child_begin = dt->child_begin;
-    sp.trie.first_label = dt->first_label;
-    sp.trie.link_off = dt->link_off;
-    sp.trie.flags = dt->flags;
-    sp.trie.tail = dt->tail;
-    sp.trie.tail_end = dt->binary_tail ? dt->tail_end : nullptr;
-    sp.trie.num_nodes = dt->num_nodes;
-    sp.trie.tail_size = dt->tail_size;
+    sp.trie = ftb::make_trie_view(*dt);
     sp.meta = reinterpret_cast<const ftb::ReqMeta *>(base + a.meta);
     sp.beams = b->beams;
     sp.topk_id = b->topk_id;

@@ -28,6 +28,7 @@
 // After the last step the pool is sorted and written ascending with each
 // sequence rebuilt from the history (tbs-kernels.cu:393-474).
 #include <cooperative_groups.h>
+#include <cooperative_groups/reduce.h>
 
 #include "cuda_util.hpp"
 #include "tbs_kernel.cuh"
@@ -44,6 +45,8 @@ constexpr int kRadixBins = 1 << kRadixBits;
 constexpr int kKeyBits = 192;
 constexpr int kNodeFlagTerminal = 1;
 constexpr int kNodeFlagLink = 2;
+constexpr int kNodeFlagHashed = 4;    // plain nodes
+constexpr int kNodeFlagLinkEnds1 = 4;  // link nodes
 
 // ------------------------------------------------------------- keys
 // Monotone map of an f64 to u64 (-0.0 folded onto +0.0).
@@ -107,8 +110,12 @@ struct SharedState {
   uint32_t n_next;              // candidates of this step
   uint32_t pool_n;              // pool entries kept from earlier steps
   uint32_t pool_end;            // pool entries after this step's appends
-  uint32_t br_cursor;           // branching-beam queue
+  uint32_t n_tasks;             // branching-expansion tasks of the current chunk
+  uint32_t n_hits;              // lookup hits of the current chunk
+  uint32_t task_cursor;
   uint32_t eq_taken;
+  unsigned long long key_min;   // range of the candidates' first key word
+  unsigned long long key_max;
   uint32_t cur;                 // current beam buffer
   uint64_t sel_pushes;          // pushes to the pool so far (early exit)
   // radix select
@@ -121,6 +128,13 @@ struct SharedState {
   uint32_t warp_sums[kWarps];
   uint32_t hist[kRadixBins];
   unsigned long long t_exp, t_sel, t_ovh, t_start;
+};
+
+// Task table of a chunk of branching parents, in dynamic shared memory.
+struct BranchTable {
+  uint4 *info;     // c0, fan-out, hash base, mode | lg << 8
+  double *score;   // parent score
+  uint32_t *start; // first task of each parent
 };
 
 // Row of the current step, in dynamic shared memory.
@@ -167,11 +181,26 @@ struct Ctx {
   SharedState *S;
   RowView row;
   const Beam *cur;
-  uint32_t step;  // t
+  uint32_t step;   // t
+  double f_next;   // length-norm factor of the candidates' depth (t + 1)
 };
+
+__device__ __forceinline__ uint32_t block_exclusive_sum(uint32_t v, SharedState *S);
 
 __device__ __forceinline__ void push_next(const Ctx &c, double score, uint32_t node, uint32_t off, uint32_t parent,
                                           uint32_t token) {
+  {
+    // Track the range of the first key word so the selection can skip the
+    // bits every candidate shares.
+    cg::coalesced_group g = cg::coalesced_threads();
+    const unsigned long long k1 = orderable(score * c.f_next);
+    const unsigned long long mn = cg::reduce(g, k1, cg::less<unsigned long long>());
+    const unsigned long long mx = cg::reduce(g, k1, cg::greater<unsigned long long>());
+    if (g.thread_rank() == 0) {
+      atomicMin(&c.S->key_min, mn);
+      atomicMax(&c.S->key_max, mx);
+    }
+  }
   const uint32_t i = append_slot(&c.S->n_next);
   if (i < c.p->cand_cap) {
     Cand v;
@@ -210,31 +239,6 @@ __device__ __forceinline__ bool tail_ends_at(const TrieView &t, uint32_t off, bo
   }
   ok = (uint64_t)off + 1 < t.tail_size;
   return ok ? (__ldg(t.tail + off + 1) == kTailTerm) : true;
-}
-
-// A child `c` of a branching beam matched proposal log-prob `lp`.
-__device__ __forceinline__ void emit_branch_child(const Ctx &c, const Beam &b, uint32_t parent_idx, uint32_t child,
-                                                  uint32_t label, double score) {
-  const TrieView &t = c.p->trie;
-  const uint8_t f = __ldg(t.flags + child);
-  if (!(f & kNodeFlagLink)) {
-    push_next(c, score, child, kNoOffset, parent_idx, label);
-    if (f & kNodeFlagTerminal) push_pool(c, score, child, parent_idx, label);
-    return;
-  }
-  // Link child: its first tail token was consumed (tbs-kernels.cu:264-268).
-  const uint32_t off = __ldg(t.link_off + child);
-  bool ok;
-  const bool end = tail_ends_at(t, off, ok);
-  if (!ok) {
-    atomicOr(c.p->status, kStatusTailBounds);
-    return;
-  }
-  if (end) {
-    if (f & kNodeFlagTerminal) push_pool(c, score, child, parent_idx, label);
-  } else {
-    push_next(c, score, child, off + 1, parent_idx, label);
-  }
 }
 
 __device__ void expand_inlink(const Ctx &c) {
@@ -278,59 +282,249 @@ __device__ void expand_inlink(const Ctx &c) {
   }
 }
 
-__device__ void expand_branch(const Ctx &c) {
+// Expansion mode of a branching parent (per chunk, in shared memory).
+constexpr uint32_t kModeScan = 0;  // every child looks its label up in the row
+constexpr uint32_t kModeHash = 1;  // every proposal probes the parent's hash table
+constexpr uint32_t kModeBin = 2;   // every proposal binary-searches the child labels
+constexpr uint32_t kItemsPerLane = kTaskItems / 32;
+
+// Chooses how a parent of fan-out d is intersected with a row of K proposals:
+// the shorter side is iterated; a large fan-out uses the node's hash table
+// (one probe per proposal), or a binary search when it has none.
+__device__ __forceinline__ uint32_t pick_mode(uint32_t d, uint32_t K, uint8_t f) {
+  if (d <= 2u * K + 32u) return kModeScan;
+  if (f & kNodeFlagHashed) return kModeHash;
+  return kModeBin;
+}
+
+// Records a child found for parent q (chunk-local) and sorted-row column m.
+__device__ __forceinline__ void push_hit(const Ctx &c, uint32_t child, uint32_t q, uint32_t m) {
+  const uint32_t i = append_slot(&c.S->n_hits);
+  if (i < c.p->cand_cap) {
+    c.slot.hits[i] = Hit{child, (q << 16) | m};
+  } else {
+    atomicOr(c.p->status, kStatusCandOverflow);
+  }
+}
+
+// Lookup tasks.  All loads of a lane's items are issued before any is used.
+__device__ __forceinline__ void task_scan(const Ctx &c, uint32_t c0, uint32_t d, uint32_t first_item, double score,
+                                          uint32_t q) {
   const TrieView &t = c.p->trie;
   const double tt = c.p->token_threshold, st = c.p->sent_threshold;
+  const uint32_t lane = threadIdx.x & 31;
+  uint32_t lab[kItemsPerLane];
+#pragma unroll
+  for (uint32_t k = 0; k < kItemsPerLane; ++k) {
+    const uint32_t i = first_item + 32u * k + lane;
+    lab[k] = i < d ? __ldg(t.first_label + c0 + i) : 0u;
+  }
+#pragma unroll
+  for (uint32_t k = 0; k < kItemsPerLane; ++k) {
+    const uint32_t i = first_item + 32u * k + lane;
+    if (i >= d) continue;
+    for (uint32_t m = row_lower_bound(c.row, lab[k]); m < c.row.K && c.row.id[m] == lab[k]; ++m) {
+      const double lp = (double)c.row.lp[m];
+      if (lp <= tt || score + lp <= st) continue;
+      push_hit(c, c0 + i, q, m);
+    }
+  }
+}
+
+__device__ __forceinline__ void task_hash(const Ctx &c, uint32_t base, uint32_t lg, uint32_t first_item, double score,
+                                          uint32_t q) {
+  const TrieView &t = c.p->trie;
+  const double tt = c.p->token_threshold, st = c.p->sent_threshold;
+  const uint32_t lane = threadIdx.x & 31;
+  const uint32_t mask = (1u << lg) - 1u;
+  uint32_t x[kItemsPerLane], h[kItemsPerLane];
+  uint2 slot[kItemsPerLane];
+  bool on[kItemsPerLane];
+#pragma unroll
+  for (uint32_t k = 0; k < kItemsPerLane; ++k) {
+    const uint32_t m = first_item + 32u * k + lane;
+    on[k] = false;
+    x[k] = 0;
+    h[k] = 0;
+    if (m < c.row.K) {
+      const double lp = (double)c.row.lp[m];
+      x[k] = c.row.id[m];
+      on[k] = !(lp <= tt || score + lp <= st);
+    }
+    if (on[k]) {
+      h[k] = (x[k] * 2654435761u) >> (32 - lg);
+      slot[k] = __ldg(t.hash + base + h[k]);
+    }
+  }
+#pragma unroll
+  for (uint32_t k = 0; k < kItemsPerLane; ++k) {
+    if (!on[k]) continue;
+    uint2 sl = slot[k];
+    uint32_t hk = h[k];
+    while (sl.y != 0 && sl.x != x[k]) {
+      hk = (hk + 1) & mask;
+      sl = __ldg(t.hash + base + hk);
+    }
+    if (sl.y != 0) push_hit(c, sl.y, q, first_item + 32u * k + lane);
+  }
+}
+
+__device__ __forceinline__ void task_bin(const Ctx &c, uint32_t c0, uint32_t d, uint32_t first_item, double score,
+                                         uint32_t q) {
+  const TrieView &t = c.p->trie;
+  const double tt = c.p->token_threshold, st = c.p->sent_threshold;
+  const uint32_t lane = threadIdx.x & 31;
+  const uint32_t *labs = t.first_label + c0;
+#pragma unroll
+  for (uint32_t k = 0; k < kItemsPerLane; ++k) {
+    const uint32_t m = first_item + 32u * k + lane;
+    if (m >= c.row.K) continue;
+    const double lp = (double)c.row.lp[m];
+    if (lp <= tt || score + lp <= st) continue;
+    const uint32_t xv = c.row.id[m];
+    uint32_t lo = 0, n = d;
+    while (n > 0) {
+      const uint32_t half = n >> 1;
+      if (__ldg(labs + lo + half) < xv) {
+        lo += half + 1;
+        n -= half + 1;
+      } else {
+        n = half;
+      }
+    }
+    if (lo < d && __ldg(labs + lo) == xv) push_hit(c, c0 + lo, q, m);
+  }
+}
+
+// Turns the hits of a chunk into candidates: one flags/link_off gather per
+// hit, issued for two hits at a time (tbs-kernels.cu:295-317).
+__device__ void resolve_hits(const Ctx &c, const BranchTable &bt, uint32_t c_first, uint32_t n_hits) {
+  const TrieView &t = c.p->trie;
+  const uint32_t beam_cap = c.p->beam_cap;
+  for (uint32_t i0 = threadIdx.x; i0 < n_hits; i0 += 2 * blockDim.x) {
+    Hit hv[2];
+    uint8_t f[2];
+    uint32_t lo[2];
+    bool ok[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const uint32_t i = i0 + k * blockDim.x;
+      ok[k] = i < n_hits;
+      if (ok[k]) {
+        hv[k] = c.slot.hits[i];
+        f[k] = __ldg(t.flags + hv[k].child);
+        lo[k] = __ldg(t.link_off + hv[k].child);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      if (!ok[k]) continue;
+      const uint32_t q = hv[k].qm >> 16, m = hv[k].qm & 0xFFFFu;
+      const double score = bt.score[q] + (double)c.row.lp[m];
+      const uint32_t token = c.row.id[m];
+      const uint32_t parent_idx = beam_cap - 1 - (c_first + q);
+      const uint32_t child = hv[k].child;
+      if (!(f[k] & kNodeFlagLink)) {
+        push_next(c, score, child, kNoOffset, parent_idx, token);
+        if (f[k] & kNodeFlagTerminal) push_pool(c, score, child, parent_idx, token);
+      } else if (f[k] & kNodeFlagLinkEnds1) {
+        // The link's string ended with its first token (tbs-kernels.cu:310-313).
+        if (f[k] & kNodeFlagTerminal) push_pool(c, score, child, parent_idx, token);
+      } else {
+        push_next(c, score, child, lo[k] + 1, parent_idx, token);
+      }
+    }
+  }
+}
+
+// Branching beams, per chunk of parents: (1) mode and task count per parent,
+// (2) every warp drains a task table of (parent, 128 items) doing lookups
+// only, (3) all threads resolve the hits.  A heavy parent is spread over all
+// warps, and the dependent gathers of a match happen in one bulk round.
+__device__ void expand_branch(const Ctx &c, const BranchTable &bt) {
+  const TrieView &t = c.p->trie;
   const uint32_t lane = threadIdx.x & 31;
   const uint32_t n_br = c.S->n_br;
   const uint32_t K = c.row.K;
   const uint32_t beam_cap = c.p->beam_cap;
-  for (;;) {
-    uint32_t q = 0;
-    if (lane == 0) q = atomicAdd(&c.S->br_cursor, 1u);
-    q = __shfl_sync(0xFFFFFFFFu, q, 0);
-    if (q >= n_br) break;
-    const uint32_t idx = beam_cap - 1 - q;
-    const Beam b = c.cur[idx];
-    if ((uint64_t)b.node >= t.num_nodes) {
-      if (lane == 0) atomicOr(c.p->status, kStatusNodeBounds);
-      continue;
+  for (uint32_t c_first = 0; c_first < n_br; c_first += kParentChunk) {
+    const uint32_t m = min(kParentChunk, n_br - c_first);
+    uint32_t my_tasks[kParentChunk / kSearchThreads];
+#pragma unroll
+    for (uint32_t r = 0; r < kParentChunk / kSearchThreads; ++r) {
+      const uint32_t q = threadIdx.x * (kParentChunk / kSearchThreads) + r;
+      my_tasks[r] = 0;
+      if (q >= m) continue;
+      const uint32_t idx = beam_cap - 1 - (c_first + q);
+      const Beam b = c.cur[idx];
+      uint4 info = make_uint4(0, 0, 0, 0);
+      if ((uint64_t)b.node >= t.num_nodes) {
+        atomicOr(c.p->status, kStatusNodeBounds);
+      } else {
+        const uint32_t c0 = __ldg(t.child_begin + b.node);
+        const uint32_t c1 = __ldg(t.child_begin + b.node + 1);
+        const uint32_t d = c1 > c0 ? c1 - c0 : 0;
+        uint8_t f = 0;
+        uint32_t hbase = 0;
+        if (d > 2u * K + 32u) {
+          f = __ldg(t.flags + b.node);
+          if (f & kNodeFlagHashed) hbase = __ldg(t.link_off + b.node);
+        }
+        const uint32_t mode = pick_mode(d, K, f);
+        const uint32_t items = (d == 0) ? 0u : (mode == kModeScan ? d : K);
+        info = make_uint4(c0, d, hbase, mode | ((uint32_t)(f >> 3) << 8));
+        my_tasks[r] = (items + kTaskItems - 1) / kTaskItems;
+      }
+      bt.info[q] = info;
+      bt.score[q] = b.score;
     }
-    const uint32_t c0 = __ldg(t.child_begin + b.node);
-    const uint32_t c1 = __ldg(t.child_begin + b.node + 1);
-    if (c1 <= c0) continue;
-    const uint32_t d = c1 - c0;
-    if (d <= 8u * K + 64u) {
-      // Small fan-out: every child looks its label up in the sorted row.
-      for (uint32_t ch = c0 + lane; ch < c1; ch += 32) {
-        const uint32_t lab = __ldg(t.first_label + ch);
-        uint32_t m = row_lower_bound(c.row, lab);
-        for (; m < K && c.row.id[m] == lab; ++m) {
-          const double lp = (double)c.row.lp[m];
-          if (lp <= tt || b.score + lp <= st) continue;
-          emit_branch_child(c, b, idx, ch, lab, b.score + lp);
+    uint32_t sum = 0;
+#pragma unroll
+    for (uint32_t r = 0; r < kParentChunk / kSearchThreads; ++r) sum += my_tasks[r];
+    uint32_t pre = block_exclusive_sum(sum, c.S);
+#pragma unroll
+    for (uint32_t r = 0; r < kParentChunk / kSearchThreads; ++r) {
+      const uint32_t q = threadIdx.x * (kParentChunk / kSearchThreads) + r;
+      if (q < m) bt.start[q] = pre;
+      pre += my_tasks[r];
+    }
+    if (threadIdx.x == blockDim.x - 1) {
+      c.S->n_tasks = pre;
+      c.S->task_cursor = 0;
+      c.S->n_hits = 0;
+    }
+    __syncthreads();
+    const uint32_t total = c.S->n_tasks;
+    for (;;) {
+      uint32_t task = 0;
+      if (lane == 0) task = atomicAdd(&c.S->task_cursor, 1u);
+      task = __shfl_sync(0xFFFFFFFFu, task, 0);
+      if (task >= total) break;
+      uint32_t lo = 0, n = m;  // last parent whose first task <= task
+      while (n > 1) {
+        const uint32_t half = n >> 1;
+        if (bt.start[lo + half] <= task) {
+          lo += half;
+          n -= half;
+        } else {
+          n = half;
         }
       }
-    } else {
-      // Large fan-out: every proposal binary-searches the child labels.
-      const uint32_t *labs = t.first_label + c0;
-      for (uint32_t m = lane; m < K; m += 32) {
-        const double lp = (double)c.row.lp[m];
-        if (lp <= tt || b.score + lp <= st) continue;
-        const uint32_t x = c.row.id[m];
-        uint32_t lo = 0, n = d;
-        while (n > 0) {
-          const uint32_t half = n >> 1;
-          if (__ldg(labs + lo + half) < x) {
-            lo += half + 1;
-            n -= half + 1;
-          } else {
-            n = half;
-          }
-        }
-        if (lo < d && __ldg(labs + lo) == x) emit_branch_child(c, b, idx, c0 + lo, x, b.score + lp);
+      const uint4 info = bt.info[lo];
+      const double score = bt.score[lo];
+      const uint32_t first_item = (task - bt.start[lo]) * kTaskItems;
+      const uint32_t mode = info.w & 0xFFu;
+      if (mode == kModeScan) {
+        task_scan(c, info.x, info.y, first_item, score, lo);
+      } else if (mode == kModeHash) {
+        task_hash(c, info.z, info.w >> 8, first_item, score, lo);
+      } else {
+        task_bin(c, info.x, info.y, first_item, score, lo);
       }
     }
+    __syncthreads();
+    resolve_hits(c, bt, c_first, min(c.S->n_hits, (uint32_t)c.p->cand_cap));
+    __syncthreads();
   }
 }
 
@@ -364,19 +558,20 @@ __device__ __forceinline__ uint32_t block_exclusive_sum(uint32_t v, SharedState 
 // Exact top-k threshold over n candidates by the 192-bit key.  On return
 // S->sel_ge says whether every key >= sel_prefix is taken (exactly k of
 // them), or keys > sel_prefix plus the first sel_rem keys equal to it.
+// `start` leading bits of the first key word are known to be common to all
+// n keys (equal to those of `common_w0`); the passes begin after them.
 template <bool kPoolKeys>
 __device__ void radix_select(const Cand *v, uint32_t n, uint32_t k, const double *factor, uint32_t depth_const,
-                             SharedState *S) {
+                             SharedState *S, int start = 0, uint64_t common_w0 = 0) {
   if (threadIdx.x == 0) {
-    S->sel_prefix = Key3{{0, 0, 0}};
-    S->sel_mask = Key3{{0, 0, 0}};
+    const uint64_t m0 = start >= 64 ? ~0ull : (start == 0 ? 0ull : ~0ull << (64 - start));
+    S->sel_prefix = Key3{{common_w0 & m0, 0, 0}};
+    S->sel_mask = Key3{{m0, 0, 0}};
     S->sel_rem = k;
     S->sel_ge = 0;
   }
   __syncthreads();
-  const int passes = (kKeyBits + kRadixBits - 1) / kRadixBits;
-  for (int pass = 0; pass < passes; ++pass) {
-    const int from_top = pass * kRadixBits;
+  for (int from_top = start; from_top < kKeyBits; from_top += kRadixBits) {
     const int width = min(kRadixBits, kKeyBits - from_top);
     for (int b = threadIdx.x; b < kRadixBins; b += blockDim.x) S->hist[b] = 0;
     __syncthreads();
@@ -445,7 +640,11 @@ __device__ void materialize_next(const Ctx &c, uint32_t n, uint32_t k, Beam *out
   const uint32_t depth = c.step + 1;
   const double f = c.p->factor[depth];
   const bool all = n <= k;
-  if (!all && k > 0) radix_select<false>(c.slot.next, n, k, c.p->factor, depth, S);
+  if (!all && k > 0) {
+    const uint64_t lo = S->key_min, hi = S->key_max;
+    const int common = (lo == hi) ? 64 : __clzll((long long)(lo ^ hi));
+    radix_select<false>(c.slot.next, n, k, c.p->factor, depth, S, common, lo);
+  }
   if (k == 0) return;
   const uint32_t beam_cap = c.p->beam_cap;
   Hist *hist = c.slot.hist + (uint64_t)depth * beam_cap;
@@ -599,6 +798,13 @@ __device__ void search_request(const SearchParams &p, uint32_t req, const SlotVi
   row.lp = reinterpret_cast<float *>(dyn + sizeof(uint32_t) * K);
   row.orig = reinterpret_cast<uint32_t *>(dyn + 2 * sizeof(uint32_t) * K);
   row.K = K;
+  BranchTable bt;
+  {
+    uint8_t *tb = dyn + ((12u * K + 15u) & ~15u);
+    bt.info = reinterpret_cast<uint4 *>(tb);
+    bt.score = reinterpret_cast<double *>(tb + sizeof(uint4) * kParentChunk);
+    bt.start = reinterpret_cast<uint32_t *>(tb + (sizeof(uint4) + sizeof(double)) * kParentChunk);
+  }
   __syncthreads();
 
   for (uint32_t t = 0; t < L; ++t) {
@@ -614,7 +820,8 @@ __device__ void search_request(const SearchParams &p, uint32_t req, const SlotVi
     if (threadIdx.x == 0) {
       S->n_next = 0;
       S->pool_end = S->pool_n;
-      S->br_cursor = 0;
+      S->key_min = ~0ull;
+      S->key_max = 0ull;
       S->n_in_new = 0;
       S->n_br_new = 0;
     }
@@ -629,8 +836,9 @@ __device__ void search_request(const SearchParams &p, uint32_t req, const SlotVi
     c.row = row;
     c.cur = slot.beams[S->cur];
     c.step = t;
+    c.f_next = p.factor[t + 1];
     expand_inlink(c);
-    expand_branch(c);
+    expand_branch(c, bt);
     __syncthreads();
     unsigned long long t2 = 0;
     if (threadIdx.x == 0) t2 = global_ns();
@@ -736,7 +944,8 @@ __global__ void row_prep_kernel(const ReqMeta *meta, const uint32_t *ids, const 
 size_t search_smem_bytes(uint32_t max_topk, uint32_t max_final_beam) {
   uint32_t P2 = 1;
   while (P2 < max_final_beam) P2 <<= 1;
-  const size_t row = (size_t)max_topk * 12;
+  const size_t row = (((size_t)max_topk * 12 + 15) & ~size_t(15)) +
+                     (size_t)kParentChunk * (sizeof(uint4) + sizeof(double) + sizeof(uint32_t));
   const size_t sort = (size_t)P2 * 16;
   return std::max<size_t>(std::max(row, sort), 16);
 }

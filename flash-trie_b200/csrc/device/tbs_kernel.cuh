@@ -6,6 +6,8 @@
 
 #include <cstdint>
 
+#include "device_trie.hpp"
+
 namespace ftb {
 
 constexpr uint32_t kNoOffset = 0xFFFFFFFFu;  // Beam::off of a beam not inside a link
@@ -54,12 +56,43 @@ struct TrieView {
   const uint8_t *flags;
   const uint32_t *tail;
   const uint64_t *tail_end;  // nullptr for a text tail
+  const uint2 *hash;         // per-node child tables {label, child}, see device_trie.hpp
   uint64_t num_nodes;
   uint64_t tail_size;
+  uint64_t hash_slots;
 };
 
+inline TrieView make_trie_view(const DeviceTrie &d) {
+  TrieView v;
+  v.child_begin = d.child_begin;
+  v.first_label = d.first_label;
+  v.link_off = d.link_off;
+  v.flags = d.flags;
+  v.tail = d.tail;
+  v.tail_end = d.binary_tail ? d.tail_end : nullptr;
+  v.hash = reinterpret_cast<const uint2 *>(d.hash);
+  v.num_nodes = d.num_nodes;
+  v.tail_size = d.tail_size;
+  v.hash_slots = d.hash_slots;
+  return v;
+}
+
+// Branching parents are expanded in chunks of this many parents (their task
+// table lives in shared memory behind the staged row).
+constexpr uint32_t kParentChunk = 1024;
+// Items (children or proposals) per expansion task: four per lane.
+constexpr uint32_t kTaskItems = 128;
+
 // Device workspace of one search slot (one in-flight request).
+// A child found by the lookup phase of expansion: child node and
+// (parent index within the chunk << 16 | proposal column in the sorted row).
+struct Hit {
+  uint32_t child;
+  uint32_t qm;
+};
+
 struct SlotView {
+  Hit *hits;         // [cand_cap]
   Cand *next;        // [cand_cap]
   Cand *pool;        // [pool_cap]
   Cand *pool_tmp;    // [beam_cap]

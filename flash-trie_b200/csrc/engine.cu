@@ -47,6 +47,7 @@ Engine::Engine(std::shared_ptr<DeviceTrie> trie, const EngineLimits &lim) : trie
   try {
     std::vector<SlotView> slots(n_slots_);
     for (uint32_t s = 0; s < n_slots_; ++s) {
+      slots[s].hits = (Hit *)dalloc(sizeof(Hit) * cand_cap);
       slots[s].next = (Cand *)dalloc(sizeof(Cand) * cand_cap);
       slots[s].pool = (Cand *)dalloc(sizeof(Cand) * pool_cap);
       slots[s].pool_tmp = (Cand *)dalloc(sizeof(Cand) * B);
@@ -116,15 +117,7 @@ void Engine::validate_request(const ft_request &r) const {
 
 void Engine::fill_params(SearchParams &sp, const ft_search_params &prm, uint32_t n_req) const {
   std::memset(&sp, 0, sizeof(sp));
-  const DeviceTrie &t = *trie_;
-  sp.trie.child_begin = t.child_begin;
-  sp.trie.first_label = t.first_label;
-  sp.trie.link_off = t.link_off;
-  sp.trie.flags = t.flags;
-  sp.trie.tail = t.tail;
-  sp.trie.tail_end = t.binary_tail ? t.tail_end : nullptr;
-  sp.trie.num_nodes = t.num_nodes;
-  sp.trie.tail_size = t.tail_size;
+  sp.trie = make_trie_view(*trie_);
   sp.row_id = d_row_id_;
   sp.row_lp = d_row_lp_;
   sp.row_orig = d_row_orig_;
