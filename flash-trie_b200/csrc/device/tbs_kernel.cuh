@@ -131,6 +131,7 @@ struct SearchParams {
   uint32_t *out_tok;
   double *out_phase_ms;  // [n_req][5] or nullptr
   uint32_t *status;      // device status word (bit flags, see kStatus*)
+  uint32_t *debug;       // [8]: first failed self-check (code, step, n, k, got, team, ge, rem)
 };
 
 constexpr uint32_t kStatusCandOverflow = 1u;
@@ -138,14 +139,23 @@ constexpr uint32_t kStatusPoolOverflow = 2u;
 constexpr uint32_t kStatusTailBounds = 4u;
 constexpr uint32_t kStatusNodeBounds = 8u;
 constexpr uint32_t kStatusBadRequest = 16u;
+constexpr uint32_t kStatusSelection = 32u;  // a selection did not select exactly k
 
 // Shared-memory bytes the search kernel needs for a given max K / max final beam.
 size_t search_smem_bytes(uint32_t max_topk, uint32_t max_final_beam);
 
-// Enqueues the row-prep kernel and the search kernel on `stream`.
-// `max_K`, `max_L` bound every request of the batch.
+// Enqueues the row-prep kernel and the search kernel on `stream`: `grid`
+// teams of `cluster_size` CTAs (thread-block clusters), one team per
+// in-flight request.  `max_K`, `max_L` bound every request of the batch.
 void launch_search(const SearchParams &p, uint32_t max_K, uint32_t max_L, size_t smem_bytes, int grid,
-                   cudaStream_t stream);
+                   cudaStream_t stream, int cluster_size);
+
+// Teams of `cluster_size` CTAs that can be resident at once.
+int max_search_clusters(int cluster_size, size_t smem_bytes);
+
+// Team size for a batch of n requests: the largest power of two <= 16 with
+// n teams fitting on the device (FT_CLUSTER_SIZE overrides).
+int pick_cluster_size(uint32_t n, size_t smem_bytes, int *max_teams);
 
 // Configures kernel attributes once per device; returns max resident search CTAs.
 int configure_search_kernel(size_t smem_bytes);

@@ -39,7 +39,7 @@ Engine::Engine(std::shared_ptr<DeviceTrie> trie, const EngineLimits &lim) : trie
     throw InvalidArgument("init_tbs_gpu: max_num_out_beams must be in [1, " + std::to_string(kMaxBeams) + "]");
   CUDA_TRY(cudaGetDevice(&device_));
   smem_ = search_smem_bytes((uint32_t)lim.max_topk, (uint32_t)lim.max_out_beams);
-  max_ctas_ = configure_search_kernel(smem_);
+  max_ctas_ = ensure_search_smem(smem_, 64 * 1024);
   n_slots_ = (uint32_t)std::min<uint64_t>(lim.max_batch, (uint64_t)max_ctas_);
 
   const uint64_t B = lim.max_out_beams, K = lim.max_topk, L = lim.max_outpos, NB = lim.max_batch;
@@ -62,6 +62,10 @@ Engine::Engine(std::shared_ptr<DeviceTrie> trie, const EngineLimits &lim) : trie
     d_row_orig_ = (uint32_t *)dalloc(4 * NB * L * K);
     d_status_ = (uint32_t *)dalloc(16);
     CUDA_TRY(cudaMemset(d_status_, 0, 16));
+    d_status_dev_ = (uint32_t *)dalloc(16);
+    CUDA_TRY(cudaMemset(d_status_dev_, 0, 16));
+    d_debug_ = (uint32_t *)dalloc(64);
+    CUDA_TRY(cudaMemset(d_debug_, 0, 64));
 
     in_bytes_ = align16(sizeof(ReqMeta) * NB) + align16(8 * (L + 1)) + align16(4 * NB * L) + 2 * align16(4 * NB * L * K);
     d_in_ = (uint8_t *)dalloc(in_bytes_);
@@ -133,6 +137,7 @@ void Engine::fill_params(SearchParams &sp, const ft_search_params &prm, uint32_t
   sp.sent_threshold = prm.sent_logp_threshold;
   sp.early_exit = prm.early_exit ? 1 : 0;
   sp.status = d_status_;
+  sp.debug = d_debug_;
 }
 
 void Engine::search_host(const ft_request *reqs, uint32_t n, const ft_search_params &prm, ft_result *out) {
@@ -204,16 +209,23 @@ void Engine::search_host(const ft_request *reqs, uint32_t n, const ft_search_par
   sp.out_lpn = reinterpret_cast<double *>(d_out_ + q_lpn);
   sp.out_len = reinterpret_cast<uint32_t *>(d_out_ + q_len);
   sp.out_tok = reinterpret_cast<uint32_t *>(d_out_ + q_tok);
-  const int grid = (int)std::min<uint32_t>(n, n_slots_);
-  launch_search(sp, max_K, max_L, smem_, grid, stream_);
+  int max_teams = 1;
+  const int cs = pick_cluster_size(n, smem_, &max_teams);
+  const int grid = (int)std::min<uint32_t>(std::min<uint32_t>(n, n_slots_), (uint32_t)max_teams);
+  launch_search(sp, max_K, max_L, smem_, grid, stream_, cs);
   CUDA_TRY(cudaMemcpyAsync(d_out_, d_status_, 4, cudaMemcpyDeviceToDevice, stream_));
   CUDA_TRY(cudaMemcpyAsync(h_out_, d_out_, out_used, cudaMemcpyDeviceToHost, stream_));
   CUDA_TRY(cudaStreamSynchronize(stream_));
 
   const uint32_t status = *reinterpret_cast<const uint32_t *>(h_out_);
-  if (status != 0)
-    throw std::runtime_error("tbs: the search kernel reported a failed bounds check (status 0x" +
-                             std::to_string(status) + "); the trie image or workspace is inconsistent");
+  if (status != 0) {
+    uint32_t dbg[8] = {0};
+    CUDA_TRY(cudaMemcpy(dbg, d_debug_, sizeof(dbg), cudaMemcpyDeviceToHost));
+    std::string d;
+    for (int i = 0; i < 8; ++i) d += (i ? "," : "") + std::to_string(dbg[i]);
+    throw std::runtime_error("tbs: the search kernel reported a failed self-check (status " + std::to_string(status) +
+                             ", detail " + d + ")");
+  }
   const uint32_t *hcount = reinterpret_cast<const uint32_t *>(h_out_ + q_count);
   const double *hphase = reinterpret_cast<const double *>(h_out_ + q_phase);
   const double *hlpn = reinterpret_cast<const double *>(h_out_ + q_lpn);
@@ -267,9 +279,11 @@ void Engine::search_device(const ft_device_batch &b, const ft_search_params &prm
   sp.out_len = b.out_len;
   sp.out_tok = b.out_tok;
   sp.out_phase_ms = nullptr;
-  const int grid = (int)std::min<uint32_t>(b.n, n_slots_);
-  CUDA_TRY(cudaMemsetAsync(d_status_, 0, 4, stream));
-  launch_search(sp, K, L, smem_, grid, stream);
+  sp.status = d_status_dev_;
+  int max_teams = 1;
+  const int cs = pick_cluster_size(b.n, smem_, &max_teams);
+  const int grid = (int)std::min<uint32_t>(std::min<uint32_t>(b.n, n_slots_), (uint32_t)max_teams);
+  launch_search(sp, K, L, smem_, grid, stream, cs);
 }
 
 uint32_t Engine::read_status() {
@@ -277,7 +291,8 @@ uint32_t Engine::read_status() {
   uint32_t s = 0;
   CUDA_TRY(cudaSetDevice(device_));
   CUDA_TRY(cudaDeviceSynchronize());
-  CUDA_TRY(cudaMemcpy(&s, d_status_, 4, cudaMemcpyDeviceToHost));
+  CUDA_TRY(cudaMemcpy(&s, d_status_dev_, 4, cudaMemcpyDeviceToHost));
+  CUDA_TRY(cudaMemset(d_status_dev_, 0, 4));
   return s;
 }
 

@@ -72,7 +72,9 @@ class Engine {
   uint32_t *d_row_id_ = nullptr;
   float *d_row_lp_ = nullptr;
   uint32_t *d_row_orig_ = nullptr;
-  uint32_t *d_status_ = nullptr;
+  uint32_t *d_status_ = nullptr;      // host-buffer path: cleared per call
+  uint32_t *d_status_dev_ = nullptr;  // device path: accumulates until read
+  uint32_t *d_debug_ = nullptr;       // first failed kernel self-check
   // staging: [meta | factor | beams | ids | logp] on device and pinned host
   uint8_t *d_in_ = nullptr;
   uint8_t *h_in_ = nullptr;

@@ -158,8 +158,9 @@ typedef struct {
 int ft_tbs_batch_device(ft_trie *trie, const ft_device_batch *batch,
                         const ft_search_params *params, void *stream);
 
-/* Status word of the last device search (0 = clean); a non-zero value names
- * the first bounds check that failed inside the kernel. */
+/* Status word of the device-resident searches since the last call (0 =
+ * clean; the word is cleared by reading it); non-zero bits name the checks
+ * that failed inside the kernel. */
 int ft_trie_device_status(ft_trie *trie, uint32_t *status);
 
 /*
