@@ -42,6 +42,7 @@ for _p in (REPO, PKG):
         sys.path.insert(0, _p)
 
 import workload as W  # noqa: E402
+from flashtrie_shard import max_over_ranks  # noqa: E402
 
 METRIC = "trie-search q/s (latency mean/p99 ms alongside); beam search over the synthetic trie of the named config"
 UNIT = "requests/s"
@@ -438,11 +439,7 @@ def run_b200(args, cfg):
     e2e_s = time.perf_counter() - t0
     h2d_step = nb * (L * 4 + L * K * 8 + 24) + 8 * (L + 1)
 
-    if world > 1:
-        import torch.distributed as dist
-        t = torch.tensor([elapsed_ms, e2e_s], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed_ms, e2e_s = float(t[0]), float(t[1])
+    elapsed_ms, e2e_s = max_over_ranks([elapsed_ms, e2e_s], device=dev)
 
     if rank == 0:
         total_req = args.steps * nb * world

@@ -176,34 +176,44 @@ def gen_keys_torch(n, vocab, len_lo, len_hi, zipf_s, seed, device="cuda"):
     cdf /= cdf[-1].clone()
     width = len_hi
     cols = torch.arange(width, device=dev)
-    mats, lens_l = [], []
-    total = 0
+    mats, lens_l, hashes = [], [], []
     keep = None
     m = int(n * 1.1) + 4096
+    chunk = 32 << 20  # rows drawn per call; bounds the f64 scratch at 10^8+ keys
     while True:
-        lens = torch.randint(len_lo, len_hi + 1, (m,), generator=g, device=dev)
-        u = torch.rand(m * width, generator=g, device=dev, dtype=torch.float64)
-        mat = torch.searchsorted(cdf, u, right=True).clamp_(max=vocab - 1).view(m, width)
-        mat.masked_fill_(cols[None, :] >= lens[:, None], 0)
-        mats.append(mat)
-        lens_l.append(lens)
-        total += m
-        allm = torch.cat(mats)
-        alll = torch.cat(lens_l)
-        h = alll.to(torch.int64) * 1000003
-        for c in range(width):
-            h = (h ^ allm[:, c]) * 1099511628211 + 7
+        for c0 in range(0, m, chunk):
+            mc = min(chunk, m - c0)
+            lens = torch.randint(len_lo, len_hi + 1, (mc,), generator=g, device=dev)
+            u = torch.rand(mc * width, generator=g, device=dev, dtype=torch.float64)
+            mat = torch.searchsorted(cdf, u, right=True).clamp_(max=vocab - 1).view(mc, width)
+            del u
+            mat.masked_fill_(cols[None, :] >= lens[:, None], 0)
+            h = lens.to(torch.int64) * 1000003
+            for c in range(width):
+                h = (h ^ mat[:, c]) * 1099511628211 + 7
+            mats.append(mat.to(torch.int32))
+            lens_l.append(lens.to(torch.int32))
+            hashes.append(h)
+            del mat
+        h = torch.cat(hashes)
         hs, perm = torch.sort(h, stable=True)
+        del h
         first = torch.ones_like(hs, dtype=torch.bool)
         first[1:] = hs[1:] != hs[:-1]
+        del hs
         keep = torch.sort(perm[first]).values
+        del perm, first
         if keep.numel() >= n:
             break
         m = int((n - keep.numel()) * 1.3) + 4096
     keep = keep[:n]
+    allm = torch.cat(mats) if len(mats) > 1 else mats[0]
+    mats.clear()
+    alll = torch.cat(lens_l)
     mat = allm[keep]
-    lens = alll[keep]
+    del allm
+    lens = alll[keep].to(torch.int64)
     offsets = torch.zeros(n + 1, dtype=torch.int64, device=dev)
     torch.cumsum(lens, 0, out=offsets[1:])
-    tokens = mat[cols[None, :] < lens[:, None]].to(torch.int64)
-    return tokens.cpu().numpy().astype(np.uint32), offsets.cpu().numpy().astype(np.uint64)
+    tokens = mat[cols[None, :] < lens[:, None]]
+    return tokens.cpu().numpy().view(np.uint32), offsets.cpu().numpy().astype(np.uint64)
