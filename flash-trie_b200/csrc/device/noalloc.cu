@@ -56,7 +56,7 @@ inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 // Byte offsets of the scratch regions for one call.
 struct Layout {
   size_t status, meta, factor, slots, rows_id, rows_lp, rows_orig, slot0, slot_bytes;
-  size_t hits, cand, pool, pool_tmp, beams0, beams1, hist;  // within a slot
+  size_t cand, pool, pool_tmp, beams0, beams1, hist;  // within a slot
   size_t total;
 };
 
@@ -79,12 +79,10 @@ Layout plan(uint32_t n, uint32_t L, uint32_t K, uint32_t B, uint32_t n_slots) {
   a.rows_orig = o;
   o = align256(o + rows);
   size_t s = 0;
-  a.hits = s;
-  s = align256(s + sizeof(ftb::Hit) * (size_t)B * K);
   a.cand = s;
   s = align256(s + sizeof(ftb::Cand) * (size_t)B * K);
   a.pool = s;
-  s = align256(s + sizeof(ftb::Cand) * ((size_t)B + (size_t)B * K));
+  s = align256(s + sizeof(ftb::Cand) * ((size_t)B + 2 * (size_t)B * K));
   a.pool_tmp = s;
   s = align256(s + sizeof(ftb::Cand) * B);
   a.beams0 = s;
@@ -117,7 +115,6 @@ __global__ void noalloc_setup_kernel(Layout a, uint32_t n, uint32_t L, uint32_t 
   for (uint32_t s = threadIdx.x; s < n_slots; s += blockDim.x) {
     unsigned char *sb = base + a.slot0 + (size_t)s * a.slot_bytes;
     ftb::SlotView v;
-    v.hits = reinterpret_cast<ftb::Hit *>(sb + a.hits);
     v.next = reinterpret_cast<ftb::Cand *>(sb + a.cand);
     v.pool = reinterpret_cast<ftb::Cand *>(sb + a.pool);
     v.pool_tmp = reinterpret_cast<ftb::Cand *>(sb + a.pool_tmp);
@@ -208,7 +205,7 @@ extern "C" int ft_tbs_batch_device_noalloc(ft_trie *trie, const ft_device_batch 
     sp.row_orig = reinterpret_cast<uint32_t *>(base + a.rows_orig);
     sp.slots = reinterpret_cast<ftb::SlotView *>(base + a.slots);
     sp.cand_cap = (uint64_t)B * K;
-    sp.pool_cap = (uint64_t)B + (uint64_t)B * K;
+    sp.pool_cap = (uint64_t)B + 2 * (uint64_t)B * K;
     sp.beam_cap = B;
     sp.n_req = n;
     sp.n_slots = n_slots;

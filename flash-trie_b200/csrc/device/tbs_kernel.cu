@@ -113,7 +113,7 @@ __device__ __forceinline__ void key_set_bits(Key3 &k, int from_top, int width, u
 }
 
 // ------------------------------------------- loads of team-written data
-// Candidates, hits, beams, pool entries and history are written by any CTA of
+// Candidates, beams, pool entries and history are written by any CTA of
 // the team and read by another after a cluster barrier; they are loaded
 // through L2 (ld.global.cg) so that no SM can see a line it cached earlier.
 __device__ __forceinline__ Cand ld_cand(const Cand *p) {
@@ -137,55 +137,56 @@ __device__ __forceinline__ Beam ld_beam(const Beam *p) {
   return b;
 }
 
-__device__ __forceinline__ Hit ld_hit(const Hit *p) {
-  const uint2 a = __ldcg(reinterpret_cast<const uint2 *>(p));
-  return Hit{a.x, a.y};
-}
-
 __device__ __forceinline__ Hist ld_hist(const Hist *p) {
   const uint2 a = __ldcg(reinterpret_cast<const uint2 *>(p));
   return Hist{a.x, a.y};
 }
 
 // ---------------------------------------------------------- team state
+// Counters of one step.  Two sets alternate by step parity: the set of step
+// t is read by every CTA after the barrier that closes step t, so the leader
+// clears it again only after the next step's expansion barrier.
+struct StepCounters {
+  uint32_t n_next;    // candidates appended
+  uint32_t key_min;   // range of the top 32 bits of the candidates' first key word
+  uint32_t key_max;
+  uint32_t n_sel;     // beams written for the next step (capped at its width)
+  uint32_t n_in_new;  // ... of which in-link
+  uint32_t n_br_new;  // ... of which branching
+  uint32_t eq_taken;  // keys equal to the selection threshold taken so far
+  uint32_t pad;
+};
+
 // Authoritative in the team's rank-0 CTA; other CTAs reach it through
 // distributed shared memory.
-struct TeamState {
-  uint32_t n_in, n_br;          // beams of the current step: in-link / branching
-  uint32_t n_sel;               // beams written for the next step (capped at its width)
-  uint32_t n_in_new, n_br_new;  // ... of which in-link / branching
-  uint32_t n_next;              // candidates of this step
-  uint32_t pool_n;              // pool entries kept from earlier steps
-  uint32_t pool_end;            // pool entries after this step's appends
-  uint32_t n_hits;              // lookup hits of this step
-  uint32_t n_compact;           // pool compaction counter
-  uint32_t eq_taken;
-  uint32_t cur;                 // current beam buffer
-  uint32_t pad0;
-  uint64_t sel_pushes;          // pushes to the pool so far (early exit)
-  uint32_t key_min;             // range of the top 32 bits of the candidates' first key word
-  uint32_t key_max;
-  Key3 sel_prefix;
-  Key3 sel_mask;
-  uint32_t sel_rem;
-  int sel_ge;                   // 1: every key >= prefix is taken
-  uint32_t hist[2][kRadixBins]; // merged histograms (double-buffered)
+struct alignas(16) TeamState {
+  StepCounters cnt[2];
+  uint32_t pool_end;       // pool entries (append counter)
+  uint32_t pool_key_min;   // range of the top 32 bits of the pool entries' first key word
+  uint32_t pool_key_max;
+  uint32_t n_compact;      // entries written by the last pool trim
+  uint32_t eq_taken_trim;
+  uint32_t pad;
+  unsigned long long removed;     // pool entries dropped by trims so far
+  uint32_t hist[3][kRadixBins];   // merged radix histograms, by pass mod 3
   unsigned long long t_exp, t_sel, t_ovh, t_start;
 };
 
-// Per-CTA state.
-struct LocalState {
+// Per-CTA state; every CTA of a team derives the same values.
+struct alignas(16) LocalState {
   uint32_t hist[kRadixBins];
   uint32_t warp_sums[kWarps];
   uint32_t n_tasks;
-  uint32_t sel_digit, sel_above;
-  // snapshots of team values, taken after a barrier
-  uint32_t n_in, n_br, cur, n_next, pool_end, pool_n, hits_lo, hits_hi;
-  uint64_t sel_pushes;
-  uint32_t key_min, key_max;
+  uint32_t sel_digit, sel_above, sel_count;
+  uint32_t n_in, n_br, n_next, pool_end;
+  uint32_t key_min, key_max, pool_key_min, pool_key_max;
+  unsigned long long pushes;
   Key3 sel_prefix;
+  Key3 sel_mask;
   uint32_t sel_rem;
   int sel_ge;
+  uint32_t pass;  // radix passes run by the team in this request
+  uint32_t stop;
 };
 
 // Task table of a chunk of branching parents, in dynamic shared memory.
@@ -206,8 +207,9 @@ struct RowView {
 struct Ctx {
   const SearchParams *p;
   SlotView slot;
-  TeamState *T;   // rank 0's team state (distributed shared memory)
-  LocalState *S;  // this CTA's state
+  TeamState *T;        // rank 0's team state (distributed shared memory)
+  StepCounters *cnt;   // this step's counters (in T)
+  LocalState *S;       // this CTA's state
   RowView row;
   const Beam *cur;
   uint32_t step;   // t
@@ -264,21 +266,23 @@ __device__ __forceinline__ uint32_t append_slot(uint32_t *counter) {
   return base + g.thread_rank();
 }
 
+// Folds this thread's value into a team-wide [min, max] of u32.
+__device__ __forceinline__ void track_range(uint32_t *mn, uint32_t *mx, uint32_t v) {
+  cg::coalesced_group g = cg::coalesced_threads();
+  const uint32_t lo = cg::reduce(g, v, cg::less<uint32_t>());
+  const uint32_t hi = cg::reduce(g, v, cg::greater<uint32_t>());
+  if (g.thread_rank() == 0) {
+    atomicMin(mn, lo);
+    atomicMax(mx, hi);
+  }
+}
+
 __device__ __forceinline__ void push_next(const Ctx &c, double score, uint32_t node, uint32_t off, uint32_t parent,
                                           uint32_t token) {
-  {
-    // Track the range of the first key word so the selection can skip the
-    // bits every candidate shares.
-    cg::coalesced_group g = cg::coalesced_threads();
-    const uint32_t k1 = (uint32_t)(orderable(score * c.f_next) >> 32);
-    const uint32_t mn = cg::reduce(g, k1, cg::less<uint32_t>());
-    const uint32_t mx = cg::reduce(g, k1, cg::greater<uint32_t>());
-    if (g.thread_rank() == 0) {
-      atomicMin(&c.T->key_min, mn);
-      atomicMax(&c.T->key_max, mx);
-    }
-  }
-  const uint32_t i = append_slot(&c.T->n_next);
+  // The range of the first key word lets the selection skip the bits every
+  // candidate shares.
+  track_range(&c.cnt->key_min, &c.cnt->key_max, (uint32_t)(orderable(score * c.f_next) >> 32));
+  const uint32_t i = append_slot(&c.cnt->n_next);
   if (i < c.p->cand_cap) {
     Cand v;
     v.score = score;
@@ -294,6 +298,7 @@ __device__ __forceinline__ void push_next(const Ctx &c, double score, uint32_t n
 
 __device__ __forceinline__ void push_pool(const Ctx &c, double score, uint32_t node, uint32_t parent,
                                           uint32_t token) {
+  track_range(&c.T->pool_key_min, &c.T->pool_key_max, (uint32_t)(orderable(score * c.f_next) >> 32));
   const uint32_t i = append_slot(&c.T->pool_end);
   if (i < c.p->pool_cap) {
     Cand v;
@@ -401,23 +406,34 @@ __device__ __forceinline__ uint32_t pick_mode(uint32_t d, uint32_t K, uint8_t f)
   return kModeBin;
 }
 
-// Records a child found for parent q (chunk-local) and sorted-row column m.
-__device__ __forceinline__ void push_hit(const Ctx &c, uint32_t child, uint32_t q, uint32_t m) {
-  const uint32_t i = append_slot(&c.T->n_hits);
-  if (i < c.p->cand_cap) {
-    c.slot.hits[i] = Hit{child, (q << 16) | m};
+// A child `child` (flags f, link offset lo) of a branching parent matched
+// sorted-row column m: the candidate and pool entry it yields
+// (tbs-kernels.cu:295-317).
+__device__ __forceinline__ void emit_child(const Ctx &c, double pscore, uint32_t parent_idx, uint32_t child,
+                                           uint8_t f, uint32_t lo, uint32_t m) {
+  const double lp = (double)c.row.lp[m];
+  if (lp <= c.p->token_threshold || pscore + lp <= c.p->sent_threshold) return;
+  const double score = pscore + lp;
+  const uint32_t token = c.row.id[m];
+  if (!(f & kNodeFlagLink)) {
+    push_next(c, score, child, kNoOffset, parent_idx, token);
+    if (f & kNodeFlagTerminal) push_pool(c, score, child, parent_idx, token);
+  } else if (f & kNodeFlagLinkEnds1) {
+    // The link's string ended with its first token (tbs-kernels.cu:310-313).
+    if (f & kNodeFlagTerminal) push_pool(c, score, child, parent_idx, token);
   } else {
-    atomicOr(c.p->status, kStatusCandOverflow);
+    push_next(c, score, child, lo + 1, parent_idx, token);
   }
 }
 
-// Lookup tasks.  All loads of a lane's items are issued before any is used.
+// Lookup tasks: a lane's four items issue each round of loads (labels or
+// probes, then the found children's flags and link offsets) before using any.
 __device__ __forceinline__ void task_scan(const Ctx &c, uint32_t c0, uint32_t d, uint32_t first_item, double score,
-                                          uint32_t q) {
+                                          uint32_t parent_idx) {
   const TrieView &t = c.p->trie;
-  const double tt = c.p->token_threshold, st = c.p->sent_threshold;
   const uint32_t lane = threadIdx.x & 31;
-  uint32_t lab[kItemsPerLane];
+  uint32_t lab[kItemsPerLane], mlo[kItemsPerLane], lo[kItemsPerLane];
+  uint8_t f[kItemsPerLane];
 #pragma unroll
   for (uint32_t k = 0; k < kItemsPerLane; ++k) {
     const uint32_t i = first_item + 32u * k + lane;
@@ -426,22 +442,33 @@ __device__ __forceinline__ void task_scan(const Ctx &c, uint32_t c0, uint32_t d,
 #pragma unroll
   for (uint32_t k = 0; k < kItemsPerLane; ++k) {
     const uint32_t i = first_item + 32u * k + lane;
-    if (i >= d) continue;
-    for (uint32_t m = row_lower_bound(c.row, lab[k]); m < c.row.K && c.row.id[m] == lab[k]; ++m) {
-      const double lp = (double)c.row.lp[m];
-      if (lp <= tt || score + lp <= st) continue;
-      push_hit(c, c0 + i, q, m);
+    mlo[k] = c.row.K;
+    if (i < d) {
+      const uint32_t m = row_lower_bound(c.row, lab[k]);
+      if (m < c.row.K && c.row.id[m] == lab[k]) mlo[k] = m;
     }
+    if (mlo[k] < c.row.K) {
+      f[k] = __ldg(t.flags + c0 + i);
+      lo[k] = __ldg(t.link_off + c0 + i);
+    }
+  }
+#pragma unroll
+  for (uint32_t k = 0; k < kItemsPerLane; ++k) {
+    if (mlo[k] >= c.row.K) continue;
+    const uint32_t child = c0 + first_item + 32u * k + lane;
+    for (uint32_t m = mlo[k]; m < c.row.K && c.row.id[m] == lab[k]; ++m)
+      emit_child(c, score, parent_idx, child, f[k], lo[k], m);
   }
 }
 
 __device__ __forceinline__ void task_hash(const Ctx &c, uint32_t base, uint32_t lg, uint32_t first_item, double score,
-                                          uint32_t q) {
+                                          uint32_t parent_idx) {
   const TrieView &t = c.p->trie;
   const double tt = c.p->token_threshold, st = c.p->sent_threshold;
   const uint32_t lane = threadIdx.x & 31;
   const uint32_t mask = (1u << lg) - 1u;
-  uint32_t x[kItemsPerLane], h[kItemsPerLane];
+  uint32_t x[kItemsPerLane], h[kItemsPerLane], child[kItemsPerLane], lo[kItemsPerLane];
+  uint8_t f[kItemsPerLane];
   uint2 slot[kItemsPerLane];
   bool on[kItemsPerLane];
 #pragma unroll
@@ -462,6 +489,7 @@ __device__ __forceinline__ void task_hash(const Ctx &c, uint32_t base, uint32_t 
   }
 #pragma unroll
   for (uint32_t k = 0; k < kItemsPerLane; ++k) {
+    child[k] = 0;
     if (!on[k]) continue;
     uint2 sl = slot[k];
     uint32_t hk = h[k];
@@ -469,89 +497,73 @@ __device__ __forceinline__ void task_hash(const Ctx &c, uint32_t base, uint32_t 
       hk = (hk + 1) & mask;
       sl = __ldg(t.hash + base + hk);
     }
-    if (sl.y != 0) push_hit(c, sl.y, q, first_item + 32u * k + lane);
+    child[k] = sl.y;
+    if (child[k] != 0) {
+      f[k] = __ldg(t.flags + child[k]);
+      lo[k] = __ldg(t.link_off + child[k]);
+    }
   }
+#pragma unroll
+  for (uint32_t k = 0; k < kItemsPerLane; ++k)
+    if (child[k] != 0) emit_child(c, score, parent_idx, child[k], f[k], lo[k], first_item + 32u * k + lane);
 }
 
 __device__ __forceinline__ void task_bin(const Ctx &c, uint32_t c0, uint32_t d, uint32_t first_item, double score,
-                                         uint32_t q) {
+                                         uint32_t parent_idx) {
   const TrieView &t = c.p->trie;
   const double tt = c.p->token_threshold, st = c.p->sent_threshold;
   const uint32_t lane = threadIdx.x & 31;
   const uint32_t *labs = t.first_label + c0;
+  uint32_t x[kItemsPerLane], pos[kItemsPerLane], lo[kItemsPerLane];
+  uint8_t f[kItemsPerLane];
+  bool on[kItemsPerLane];
 #pragma unroll
   for (uint32_t k = 0; k < kItemsPerLane; ++k) {
     const uint32_t m = first_item + 32u * k + lane;
-    if (m >= c.row.K) continue;
-    const double lp = (double)c.row.lp[m];
-    if (lp <= tt || score + lp <= st) continue;
-    const uint32_t xv = c.row.id[m];
-    uint32_t lo = 0, n = d;
-    while (n > 0) {
-      const uint32_t half = n >> 1;
-      if (__ldg(labs + lo + half) < xv) {
-        lo += half + 1;
-        n -= half + 1;
-      } else {
-        n = half;
-      }
-    }
-    if (lo < d && __ldg(labs + lo) == xv) push_hit(c, c0 + lo, q, m);
-  }
-}
-
-// Turns hits [lo, hi) into candidates: one flags/link_off gather per hit,
-// issued for two hits at a time (tbs-kernels.cu:295-317).
-__device__ void resolve_hits(const Ctx &c, const BranchTable &bt, uint32_t c_first, uint32_t lo_hit, uint32_t hi_hit) {
-  const TrieView &t = c.p->trie;
-  const uint32_t beam_cap = c.p->beam_cap;
-  const uint32_t stride = c.gthreads();
-  for (uint32_t i0 = lo_hit + c.gtid(); i0 < hi_hit; i0 += 2 * stride) {
-    Hit hv[2];
-    uint8_t f[2];
-    uint32_t lo[2];
-    bool ok[2];
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const uint32_t i = i0 + k * stride;
-      ok[k] = i < hi_hit;
-      if (ok[k]) {
-        hv[k] = ld_hit(c.slot.hits + i);
-        const uint32_t ch = (uint64_t)hv[k].child < t.num_nodes ? hv[k].child : 0u;
-        f[k] = __ldg(t.flags + ch);
-        lo[k] = __ldg(t.link_off + ch);
-      }
-    }
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      if (!ok[k]) continue;
-      const uint32_t q = hv[k].qm >> 16, m = hv[k].qm & 0xFFFFu;
-      if (q >= kParentChunk || m >= c.row.K || (uint64_t)hv[k].child >= t.num_nodes) {
-        report(c, 3, q, m, hv[k].child);
-        continue;
-      }
-      const double score = bt.score[q] + (double)c.row.lp[m];
-      const uint32_t token = c.row.id[m];
-      const uint32_t parent_idx = beam_cap - 1 - (c_first + q);
-      const uint32_t child = hv[k].child;
-      if (!(f[k] & kNodeFlagLink)) {
-        push_next(c, score, child, kNoOffset, parent_idx, token);
-        if (f[k] & kNodeFlagTerminal) push_pool(c, score, child, parent_idx, token);
-      } else if (f[k] & kNodeFlagLinkEnds1) {
-        // The link's string ended with its first token (tbs-kernels.cu:310-313).
-        if (f[k] & kNodeFlagTerminal) push_pool(c, score, child, parent_idx, token);
-      } else {
-        push_next(c, score, child, lo[k] + 1, parent_idx, token);
-      }
+    on[k] = false;
+    x[k] = 0;
+    pos[k] = 0;
+    if (m < c.row.K) {
+      const double lp = (double)c.row.lp[m];
+      x[k] = c.row.id[m];
+      on[k] = !(lp <= tt || score + lp <= st);
     }
   }
+  // Branch-free lower bounds in lockstep: every item of the task searches the
+  // same d labels, so all take the same number of steps.
+  for (uint32_t n = d; n > 1;) {
+    const uint32_t half = n >> 1;
+    uint32_t v[kItemsPerLane];
+#pragma unroll
+    for (uint32_t k = 0; k < kItemsPerLane; ++k) v[k] = __ldg(labs + pos[k] + half - 1);
+#pragma unroll
+    for (uint32_t k = 0; k < kItemsPerLane; ++k) pos[k] = v[k] < x[k] ? pos[k] + half : pos[k];
+    n -= half;
+  }
+#pragma unroll
+  for (uint32_t k = 0; k < kItemsPerLane; ++k) {
+    if (on[k] && d > 0) {
+      uint32_t p = pos[k];
+      if (__ldg(labs + p) < x[k]) ++p;
+      pos[k] = p;
+      on[k] = p < d && __ldg(labs + p) == x[k];
+    } else {
+      on[k] = false;
+    }
+    if (on[k]) {
+      f[k] = __ldg(t.flags + c0 + pos[k]);
+      lo[k] = __ldg(t.link_off + c0 + pos[k]);
+    }
+  }
+#pragma unroll
+  for (uint32_t k = 0; k < kItemsPerLane; ++k)
+    if (on[k]) emit_child(c, score, parent_idx, c0 + pos[k], f[k], lo[k], first_item + 32u * k + lane);
 }
 
 // Branching beams, per chunk of parents: every CTA builds the same task table
-// of (parent, 128 items); the team's warps drain it doing lookups only; then
-// all threads of the team resolve the hits.  A heavy parent is spread over
-// every warp of the team, and the dependent gathers of the matches happen in
-// one bulk round.
+// of (parent, 128 items) and the team's warps drain it, each task doing its
+// lookups and the gathers of what they found.  A heavy parent is spread over
+// every warp of the team; no team barrier is needed between chunks.
 __device__ void expand_branch(const Ctx &c, const BranchTable &bt) {
   const TrieView &t = c.p->trie;
   const uint32_t warp = threadIdx.x >> 5;
@@ -618,59 +630,51 @@ __device__ void expand_branch(const Ctx &c, const BranchTable &bt) {
       const double score = bt.score[lo];
       const uint32_t first_item = (task - bt.start[lo]) * kTaskItems;
       const uint32_t mode = info.w & 0xFFu;
+      const uint32_t parent_idx = beam_cap - 1 - (c_first + lo);
       if (mode == kModeScan) {
-        task_scan(c, info.x, info.y, first_item, score, lo);
+        task_scan(c, info.x, info.y, first_item, score, parent_idx);
       } else if (mode == kModeHash) {
-        task_hash(c, info.z, info.w >> 8, first_item, score, lo);
+        task_hash(c, info.z, info.w >> 8, first_item, score, parent_idx);
       } else {
-        task_bin(c, info.x, info.y, first_item, score, lo);
+        task_bin(c, info.x, info.y, first_item, score, parent_idx);
       }
     }
-    team_sync();  // every hit of the chunk is written
-    if (threadIdx.x == 0) {
-      c.S->hits_lo = c.S->hits_hi;
-      c.S->hits_hi = min(c.T->n_hits, (uint32_t)c.p->cand_cap);
-    }
-    __syncthreads();
-    // The next chunk's hits must not be appended before every CTA has taken
-    // its snapshot of this chunk's end.
-    if (c_first + kParentChunk < n_br) team_sync();
-    resolve_hits(c, bt, c_first, c.S->hits_lo, c.S->hits_hi);
     __syncthreads();  // the task table is rebuilt for the next chunk
   }
 }
 
 // ------------------------------------------------------------- selection
 // Exact top-k threshold over n candidates by the 192-bit key, computed by the
-// whole team: each CTA histograms its share of the keys and adds it into rank
-// 0's merged histogram; rank 0 picks the digit.  `start` leading bits of the
-// first key word are common to all n keys (equal to those of `common_w0`).
+// whole team with one cluster barrier per radix pass.  Each CTA histograms its
+// share of the keys that match the current prefix and adds the non-zero bins
+// into rank 0's merged histogram of this pass (buffer pass % 3); after the
+// barrier every CTA reads the merged histogram and derives the same digit.
+// While a pass fills its buffer, rank 0 zeroes the next pass's buffer, which
+// was last read before the previous barrier.  `start` leading bits of the
+// first key word are common to all n keys (equal to those of common_hi << 32).
 // On return every CTA's LocalState holds the threshold: with sel_ge every key
 // >= sel_prefix is taken (exactly k of them), otherwise keys > sel_prefix plus
 // sel_rem keys equal to it.
 template <bool kPoolKeys>
 __device__ void team_radix_select(const Ctx &c, const Cand *v, uint32_t n, uint32_t k, uint32_t depth_const,
-                                  int start, uint64_t common_w0) {
+                                  int start, uint32_t common_hi) {
   TeamState *T = c.T;
   LocalState *S = c.S;
   const double *factor = c.p->factor;
-  if (c.rank == 0) {
-    for (int b = threadIdx.x; b < kRadixBins; b += blockDim.x) T->hist[0][b] = 0;
-    if (threadIdx.x == 0) {
-      const uint64_t m0 = start >= 64 ? ~0ull : (start == 0 ? 0ull : ~0ull << (64 - start));
-      T->sel_prefix = Key3{{common_w0 & m0, 0, 0}};
-      T->sel_mask = Key3{{m0, 0, 0}};
-      T->sel_rem = k;
-      T->sel_ge = 0;
-      T->eq_taken = 0;
-    }
+  __syncthreads();  // this CTA may still be testing keys against the previous threshold
+  if (threadIdx.x == 0) {
+    const uint64_t m0 = start >= 32 ? 0xFFFFFFFF00000000ull : (start == 0 ? 0ull : ~0ull << (64 - start));
+    S->sel_prefix = Key3{{((uint64_t)common_hi << 32) & m0, 0, 0}};
+    S->sel_mask = Key3{{m0, 0, 0}};
+    S->sel_rem = k;
+    S->sel_ge = 0;
   }
-  team_sync();
-  int buf = 0;
+  __syncthreads();
   for (int from_top = start; from_top < kKeyBits; from_top += kRadixBits) {
     const int width = min(kRadixBits, kKeyBits - from_top);
+    const uint32_t buf = S->pass % 3;
     for (int b = threadIdx.x; b < kRadixBins; b += blockDim.x) S->hist[b] = 0;
-    const Key3 P = T->sel_prefix, M = T->sel_mask;
+    const Key3 P = S->sel_prefix, M = S->sel_mask;
     __syncthreads();
     for (uint32_t i = c.gtid(); i < n; i += c.gthreads()) {
       const Cand cv = ld_cand(v + i);
@@ -680,73 +684,71 @@ __device__ void team_radix_select(const Ctx &c, const Cand *v, uint32_t n, uint3
         atomicAdd(&S->hist[key_bits(key, from_top, width)], 1u);
     }
     __syncthreads();
-    if (c.cs == 1) {
-      for (int b = threadIdx.x; b < kRadixBins; b += blockDim.x) T->hist[buf][b] = S->hist[b];
-    } else {
+    if (c.cs > 1) {
       for (int b = threadIdx.x; b < kRadixBins; b += blockDim.x)
         if (S->hist[b]) atomicAdd(&T->hist[buf][b], S->hist[b]);
+      if (c.rank == 0) {
+        uint32_t *nb = T->hist[(buf + 1) % 3];
+        for (int b = threadIdx.x; b < kRadixBins; b += blockDim.x) nb[b] = 0;
+      }
     }
     team_sync();
-    if (c.rank == 0) {
-      // Bins from the top: thread i owns bins 2047-4i .. 2044-4i.
-      constexpr int kPer = kRadixBins / kSearchThreads;
-      uint32_t mine[kPer];
-      uint32_t sum = 0;
+    // Bins from the top: thread i owns bins 2047-4i .. 2044-4i.
+    constexpr int kPer = kRadixBins / kSearchThreads;
+    static_assert(kPer == 4, "one uint4 of bins per thread");
+    const uint32_t *H = c.cs > 1 ? T->hist[buf] : S->hist;
+    const uint4 q4 = *reinterpret_cast<const uint4 *>(H + kRadixBins - kPer * (threadIdx.x + 1));
+    const uint32_t mine[kPer] = {q4.w, q4.z, q4.y, q4.x};
+    const uint32_t sum = mine[0] + mine[1] + mine[2] + mine[3];
+    const uint32_t rem = S->sel_rem;
+    const uint32_t above = block_exclusive_sum(sum, S);
+    if (above < rem && rem <= above + sum) {
+      uint32_t acc = above;
 #pragma unroll
       for (int q = 0; q < kPer; ++q) {
-        mine[q] = T->hist[buf][kRadixBins - 1 - kPer * threadIdx.x - q];
-        sum += mine[q];
-      }
-      const uint32_t rem = T->sel_rem;
-      const uint32_t above = block_exclusive_sum(sum, S);
-      if (above < rem && rem <= above + sum) {
-        uint32_t acc = above;
-#pragma unroll
-        for (int q = 0; q < kPer; ++q) {
-          if (acc + mine[q] >= rem) {
-            S->sel_digit = kRadixBins - 1 - kPer * threadIdx.x - q;
-            S->sel_above = acc;
-            break;
-          }
-          acc += mine[q];
+        if (acc + mine[q] >= rem) {
+          S->sel_digit = kRadixBins - 1 - kPer * threadIdx.x - q;
+          S->sel_above = acc;
+          S->sel_count = mine[q];
+          break;
         }
+        acc += mine[q];
       }
-      for (int b = threadIdx.x; b < kRadixBins; b += blockDim.x) T->hist[buf ^ 1][b] = 0;
-      if (threadIdx.x == blockDim.x - 1 && above + sum < rem) S->sel_digit = 0xFFFFFFFFu;
-      __syncthreads();
-      if (threadIdx.x == 0 && S->sel_digit == 0xFFFFFFFFu) {
+    }
+    if (threadIdx.x == blockDim.x - 1 && above + sum < rem) S->sel_digit = 0xFFFFFFFFu;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      S->pass += 1;
+      if (S->sel_digit == 0xFFFFFFFFu) {
         // Fewer keys match the prefix than remain to be taken: the key range
         // was wrong.  Report it and take everything at or above the prefix.
         atomicOr(c.p->status, kStatusSelection);
-        T->sel_ge = 1;
-      } else if (threadIdx.x == 0) {
+        S->sel_ge = 1;
+      } else {
         const uint32_t d = S->sel_digit;
-        T->sel_rem = rem - S->sel_above;
-        key_set_bits(T->sel_prefix, from_top, width, d);
-        key_set_bits(T->sel_mask, from_top, width, low_mask(width));
-        if (T->hist[buf][d] == T->sel_rem) T->sel_ge = 1;
+        S->sel_rem = rem - S->sel_above;
+        key_set_bits(S->sel_prefix, from_top, width, d);
+        key_set_bits(S->sel_mask, from_top, width, low_mask(width));
+        if (S->sel_count == S->sel_rem) S->sel_ge = 1;
       }
     }
-    team_sync();
-    if (T->sel_ge) break;
-    buf ^= 1;
+    __syncthreads();
+    if (S->sel_ge) break;
   }
-  if (threadIdx.x == 0) {
-    S->sel_prefix = T->sel_prefix;
-    S->sel_rem = T->sel_rem;
-    S->sel_ge = T->sel_ge;
-  }
-  __syncthreads();
 }
 
 // Is `key` among the selected?  Equal keys beyond the threshold count are
 // indistinguishable beams, so which of them are taken does not matter.
-__device__ __forceinline__ bool is_selected(const Ctx &c, const Key3 &key) {
+__device__ __forceinline__ bool is_selected(const Ctx &c, const Key3 &key, uint32_t *eq_taken) {
   const int r = key_cmp(key, c.S->sel_prefix);
   if (c.S->sel_ge) return r >= 0;  // the prefix has its free bits at zero
   if (r > 0) return true;
   if (r < 0) return false;
-  return atomicAdd(&c.T->eq_taken, 1u) < c.S->sel_rem;
+  return atomicAdd(eq_taken, 1u) < c.S->sel_rem;
+}
+
+__device__ __forceinline__ int common_bits(uint32_t lo, uint32_t hi) {
+  return lo == hi ? 32 : __clz((int)(lo ^ hi));
 }
 
 // Makes the selected candidates the beams of step t+1.
@@ -755,24 +757,25 @@ __device__ void materialize_next(const Ctx &c, uint32_t n, uint32_t k, Beam *out
   const double f = c.p->factor[depth];
   const bool all = n <= k;
   if (k == 0) return;
-  if (!all) {
-    const uint32_t lo = c.S->key_min, hi = c.S->key_max;
-    const int common = (lo == hi) ? 32 : __clz((int)(lo ^ hi));
-    team_radix_select<false>(c, c.slot.next, n, k, depth, common, (uint64_t)lo << 32);
-  }
+  if (!all)
+    team_radix_select<false>(c, c.slot.next, n, k, depth, common_bits(c.S->key_min, c.S->key_max), c.S->key_min);
   const uint32_t beam_cap = c.p->beam_cap;
   Hist *hist = c.slot.hist + (uint64_t)depth * beam_cap;
   for (uint32_t i = c.gtid(); i < n; i += c.gthreads()) {
     const Cand v = ld_cand(c.slot.next + i);
-    if (!all && !is_selected(c, cand_key(v, f, depth))) continue;
-    // In-link beams fill the buffer from the front, branching beams from the
-    // back; the capped total keeps the two from ever overlapping.
-    if (atomicAdd(&c.T->n_sel, 1u) >= k) {
+    if (!all && !is_selected(c, cand_key(v, f, depth), &c.cnt->eq_taken)) continue;
+    if (append_slot(&c.cnt->n_sel) >= k) {
       atomicOr(c.p->status, kStatusSelection);
       continue;
     }
-    const bool in_link = v.aux != kNoOffset;
-    const uint32_t idx = in_link ? atomicAdd(&c.T->n_in_new, 1u) : beam_cap - 1 - atomicAdd(&c.T->n_br_new, 1u);
+    // In-link beams fill the buffer from the front, branching beams from the
+    // back; the capped total keeps the two from overlapping.
+    uint32_t idx;
+    if (v.aux != kNoOffset) {
+      idx = append_slot(&c.cnt->n_in_new);
+    } else {
+      idx = beam_cap - 1 - append_slot(&c.cnt->n_br_new);
+    }
     Beam b;
     b.score = v.score;
     b.node = v.node;
@@ -782,39 +785,33 @@ __device__ void materialize_next(const Ctx &c, uint32_t n, uint32_t k, Beam *out
   }
 }
 
-// Trims the pool to its best `k` entries; returns the entries kept.
-__device__ uint32_t trim_pool(const Ctx &c, uint32_t n, uint32_t k) {
-  if (n <= k) return n;
-  team_radix_select<true>(c, c.slot.pool, n, k, 0, 0, 0);
-  if (c.rank == 0 && threadIdx.x == 0) c.T->n_compact = 0;
-  team_sync();
+// Writes the best k of the n pool entries to pool_tmp (the team's
+// n_compact counts them).
+__device__ void trim_pool(const Ctx &c, uint32_t n, uint32_t k) {
+  team_radix_select<true>(c, c.slot.pool, n, k, 0, common_bits(c.S->pool_key_min, c.S->pool_key_max),
+                          c.S->pool_key_min);
   for (uint32_t i = c.gtid(); i < n; i += c.gthreads()) {
     const Cand v = ld_cand(c.slot.pool + i);
     if (v.aux == 0 || v.aux > c.step + 1) {
       report(c, 4, i, v.aux, c.step);
       continue;
     }
-    if (!is_selected(c, cand_key(v, c.p->factor[v.aux], v.aux))) continue;
-    const uint32_t j = atomicAdd(&c.T->n_compact, 1u);
+    if (!is_selected(c, cand_key(v, c.p->factor[v.aux], v.aux), &c.T->eq_taken_trim)) continue;
+    const uint32_t j = append_slot(&c.T->n_compact);
     if (j < k) c.slot.pool_tmp[j] = v;
   }
-  team_sync();
-  const uint32_t got = c.T->n_compact;
-  if (got != k && c.rank == 0 && threadIdx.x == 0) report(c, 2, n, k, got);
-  const uint32_t kept = min(got, k);
-  for (uint32_t i = c.gtid(); i < kept; i += c.gthreads()) c.slot.pool[i] = ld_cand(c.slot.pool_tmp + i);
-  return kept;
 }
 
 // Sorts the final pool (descending) and writes the ascending result (rank 0).
-__device__ void write_result(const SearchParams &p, const SlotView &slot, uint32_t n, uint32_t req, uint8_t *dyn) {
+__device__ void write_result(const SearchParams &p, const SlotView &slot, const Cand *pool, uint32_t n, uint32_t req,
+                             uint8_t *dyn) {
   uint32_t P2 = 1;
   while (P2 < n) P2 <<= 1;
   ulonglong2 *items = reinterpret_cast<ulonglong2 *>(dyn);
   for (uint32_t i = threadIdx.x; i < P2; i += blockDim.x) {
     ulonglong2 it = make_ulonglong2(0, 0);
     if (i < n) {
-      const Cand v = ld_cand(slot.pool + i);
+      const Cand v = ld_cand(pool + i);
       it.x = orderable(v.score * p.factor[min(v.aux, p.out_stride)]);
       it.y = ((uint64_t)v.node << 32) | ((uint64_t)(v.aux & 0xFFFFu) << 16) | (uint64_t)i;
     }
@@ -842,7 +839,7 @@ __device__ void write_result(const SearchParams &p, const SlotView &slot, uint32
   const uint32_t cap = p.out_cap, stride = p.out_stride;
   for (uint32_t s = threadIdx.x; s < n; s += blockDim.x) {
     const uint32_t idx = (uint32_t)(items[s].y & 0xFFFFu);
-    const Cand v = ld_cand(slot.pool + idx);
+    const Cand v = ld_cand(pool + idx);
     const uint32_t o = n - 1 - s;
     const uint64_t slot_o = (uint64_t)req * cap + o;
     uint32_t depth = v.aux;
@@ -868,6 +865,20 @@ __device__ void write_result(const SearchParams &p, const SlotView &slot, uint32
   if (threadIdx.x == 0) p.out_count[req] = n;
 }
 
+__device__ void reset_counters(StepCounters *s) {
+  s->n_next = 0;
+  s->key_min = 0xFFFFFFFFu;
+  s->key_max = 0;
+  s->n_sel = 0;
+  s->n_in_new = 0;
+  s->n_br_new = 0;
+  s->eq_taken = 0;
+}
+
+// One request, searched by the whole team.  Cluster barriers per step: one
+// after expansion, one per radix pass of the selection, one after the next
+// beams are written (plus the passes of a pool trim when the next step could
+// overflow the pool).
 __device__ void search_request(const SearchParams &p, uint32_t req, const SlotView &slot, TeamState *T,
                                LocalState *S, uint32_t rank, uint32_t cs, uint8_t *dyn) {
   const ReqMeta meta = p.meta[req];
@@ -908,12 +919,18 @@ __device__ void search_request(const SearchParams &p, uint32_t req, const SlotVi
     root.node = 0;
     root.off = kNoOffset;
     slot.beams[0][beam_cap - 1] = root;
-    T->n_in = 0;
-    T->n_br = 1;
-    T->cur = 0;
-    T->pool_n = 0;
-    T->sel_pushes = 0;
+    reset_counters(&T->cnt[0]);
+    reset_counters(&T->cnt[1]);
+    T->pool_end = 0;
+    T->pool_key_min = 0xFFFFFFFFu;
+    T->pool_key_max = 0;
+    T->n_compact = 0;
+    T->eq_taken_trim = 0;
+    T->removed = 0;
   }
+  if (rank == 0)
+    for (int b = threadIdx.x; b < 3 * kRadixBins; b += blockDim.x) (&T->hist[0][0])[b] = 0;
+  if (threadIdx.x == 0) S->pass = 0;
   RowView row;
   row.id = reinterpret_cast<uint32_t *>(dyn);
   row.lp = reinterpret_cast<float *>(dyn + sizeof(uint32_t) * K);
@@ -928,50 +945,63 @@ __device__ void search_request(const SearchParams &p, uint32_t req, const SlotVi
   }
   team_sync();
 
+  Ctx c;
+  c.p = &p;
+  c.slot = slot;
+  c.T = T;
+  c.S = S;
+  c.row = row;
+  c.rank = rank;
+  c.cs = cs;
+  bool trimmed = false;  // the previous step left its pool survivors in pool_tmp
+  uint32_t prev_want = 0;
   for (uint32_t t = 0; t < L; ++t) {
+    const uint32_t par = t & 1u;
     unsigned long long t0 = 0;
     if (leader) t0 = global_ns();
+    c.step = t;
+    c.cnt = &T->cnt[par];
     if (threadIdx.x == 0) {
-      S->n_in = min(T->n_in, beam_cap);
-      S->n_br = min(T->n_br, beam_cap - S->n_in);
-      S->cur = T->cur & 1u;
-      S->sel_pushes = T->sel_pushes;
-      S->pool_n = T->pool_n;
-      S->hits_lo = S->hits_hi = 0;
+      if (t == 0) {
+        S->n_in = 0;
+        S->n_br = 1;
+        S->stop = 0;
+      } else {
+        // Counters of step t-1 are final after the barrier that closed it.
+        const StepCounters *pc = &T->cnt[par ^ 1u];
+        const uint32_t sel = pc->n_sel, n_in = pc->n_in_new, n_br = pc->n_br_new;
+        S->stop = 0;
+        if (sel != prev_want || n_in + n_br != prev_want || (trimmed && T->n_compact != final_beam)) {
+          // The beam buffer or the pool is not trustworthy: stop.
+          if (rank == 0) report(c, 1, prev_want, sel, n_in + n_br);
+          S->stop = 1;
+        }
+        S->n_in = min(n_in, beam_cap);
+        S->n_br = min(n_br, beam_cap - S->n_in);
+      }
+      S->pushes = (unsigned long long)T->pool_end + T->removed;
     }
     __syncthreads();
-    if (S->n_in + S->n_br == 0 || (p.early_exit && S->sel_pushes >= final_beam)) break;
+    if (trimmed) {
+      // Survivors of the previous step's trim go back to the pool's front;
+      // this step appends behind them, and the pool is next read after the
+      // expansion barrier.
+      for (uint32_t i = c.gtid(); i < final_beam; i += c.gthreads()) slot.pool[i] = ld_cand(slot.pool_tmp + i);
+      trimmed = false;
+    }
+    if (S->stop || S->n_in + S->n_br == 0 || (p.early_exit && S->pushes >= final_beam)) break;
     const uint64_t rbase = meta.rows_off + (uint64_t)t * K;
     for (uint32_t j = threadIdx.x; j < K; j += blockDim.x) {
       row.id[j] = p.row_id[rbase + j];
       row.lp[j] = p.row_lp[rbase + j];
       row.orig[j] = p.row_orig[rbase + j];
     }
-    if (leader) {
-      T->n_next = 0;
-      T->pool_end = T->pool_n;
-      T->n_sel = 0;
-      T->n_in_new = 0;
-      T->n_br_new = 0;
-      T->n_hits = 0;
-      T->key_min = 0xFFFFFFFFu;
-      T->key_max = 0u;
-    }
-    team_sync();
+    __syncthreads();
     unsigned long long t1 = 0;
     if (leader) t1 = global_ns();
 
-    Ctx c;
-    c.p = &p;
-    c.slot = slot;
-    c.T = T;
-    c.S = S;
-    c.row = row;
-    c.cur = slot.beams[S->cur];
-    c.step = t;
+    c.cur = slot.beams[par];
     c.f_next = p.factor[t + 1];
-    c.rank = rank;
-    c.cs = cs;
     expand_inlink(c);
     expand_branch(c, bt);
     team_sync();
@@ -979,51 +1009,83 @@ __device__ void search_request(const SearchParams &p, uint32_t req, const SlotVi
     if (leader) t2 = global_ns();
 
     if (threadIdx.x == 0) {
-      S->n_next = min(T->n_next, (uint32_t)p.cand_cap);
+      S->n_next = min(c.cnt->n_next, (uint32_t)p.cand_cap);
       S->pool_end = min(T->pool_end, (uint32_t)p.pool_cap);
-      S->key_min = T->key_min;
-      S->key_max = T->key_max;
+      S->key_min = c.cnt->key_min;
+      S->key_max = c.cnt->key_max;
+      S->pool_key_min = T->pool_key_min;
+      S->pool_key_max = T->pool_key_max;
     }
     __syncthreads();
-    const uint32_t n_next = S->n_next, pool_end = S->pool_end, pool_before = S->pool_n;
-    materialize_next(c, n_next, beams[t], slot.beams[S->cur ^ 1]);
-    team_sync();
-    const uint32_t kept = trim_pool(c, pool_end, final_beam);
+    // Every CTA has read step t-1's counters and the last trim's count
+    // (before the barrier above).
+    if (leader) {
+      reset_counters(&T->cnt[par ^ 1u]);
+      T->n_compact = 0;
+      T->eq_taken_trim = 0;
+    }
+    const uint32_t n_next = S->n_next, pool_end = S->pool_end;
+    materialize_next(c, n_next, beams[t], slot.beams[par ^ 1u]);
+    prev_want = min(n_next, beams[t]);
+    // Trim the pool only when the next step's appends (at most K per beam)
+    // could overflow it.
+    if (t + 1 < L && pool_end > final_beam &&
+        (uint64_t)pool_end + (uint64_t)prev_want * K > p.pool_cap) {
+      trim_pool(c, pool_end, final_beam);
+      if (leader) {
+        T->removed += pool_end - final_beam;
+        T->pool_end = final_beam;
+      }
+      trimmed = true;
+    }
     team_sync();
     if (leader) {
-      T->sel_pushes += (uint64_t)(pool_end - pool_before);
-      T->pool_n = kept;
-      uint32_t n_in_new = T->n_in_new, n_br_new = T->n_br_new;
-      const uint32_t want = min(n_next, beams[t]);
-      if (T->n_sel != want || n_in_new + n_br_new != want) {
-        report(c, 1, n_next, beams[t], T->n_sel);
-        n_in_new = n_br_new = 0;  // the beam buffer is not trustworthy: stop
-      }
-      T->n_in = n_in_new;
-      T->n_br = n_br_new;
-      T->cur ^= 1;
       const unsigned long long t3 = global_ns();
       T->t_ovh += t1 - t0;
       T->t_exp += t2 - t1;
       T->t_sel += t3 - t2;
     }
+  }
+  // The pool survivors copied back at the last step start must land before
+  // the final trim reads the pool.
+  team_sync();
+  const unsigned long long t4 = leader ? global_ns() : 0ull;
+  if (threadIdx.x == 0) {
+    S->pool_end = min(T->pool_end, (uint32_t)p.pool_cap);
+    S->pool_key_min = T->pool_key_min;
+    S->pool_key_max = T->pool_key_max;
+  }
+  __syncthreads();
+  if (leader) {
+    // Every CTA read the last trim's count before the barrier above.
+    T->n_compact = 0;
+    T->eq_taken_trim = 0;
+  }
+  const uint32_t n_pool = S->pool_end;
+  const Cand *out_pool = slot.pool;
+  uint32_t n_out = n_pool;
+  if (n_pool > final_beam) {
+    c.step = L - 1;  // pool depths are at most L
+    trim_pool(c, n_pool, final_beam);
     team_sync();
+    out_pool = slot.pool_tmp;
+    n_out = final_beam;
+    if (threadIdx.x == 0) S->n_next = T->n_compact;
+    __syncthreads();
+    if (S->n_next != final_beam) {
+      if (leader) report(c, 2, n_pool, final_beam, S->n_next);
+      n_out = min(S->n_next, final_beam);
+    }
   }
   if (rank == 0) {
-    unsigned long long t4 = 0;
-    if (threadIdx.x == 0) {
-      t4 = global_ns();
-      S->pool_n = T->pool_n;
-    }
-    __syncthreads();
-    write_result(p, slot, S->pool_n, req, dyn);
+    write_result(p, slot, out_pool, n_out, req, dyn);
     if (threadIdx.x == 0 && p.out_phase_ms) {
       const unsigned long long t5 = global_ns();
       double *ph = p.out_phase_ms + (uint64_t)req * 5;
       ph[0] = T->t_exp * 1e-6;
       ph[1] = 0.0;  // validation is fused into expansion
-      ph[2] = T->t_sel * 1e-6;
-      ph[3] = (T->t_ovh + (t5 - t4)) * 1e-6;
+      ph[2] = (T->t_sel + (t5 - t4)) * 1e-6;
+      ph[3] = T->t_ovh * 1e-6;
       ph[4] = (t5 - T->t_start) * 1e-6;
     }
   }
@@ -1106,18 +1168,6 @@ size_t search_smem_bytes(uint32_t max_topk, uint32_t max_final_beam) {
                      (size_t)kParentChunk * (sizeof(uint4) + sizeof(double) + sizeof(uint32_t));
   const size_t sort = (size_t)P2 * 16;
   return std::max<size_t>(std::max(row, sort), 16);
-}
-
-int configure_search_kernel(size_t smem_bytes) {
-  CUDA_TRY(cudaFuncSetAttribute(tbs_search_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes));
-  CUDA_TRY(cudaFuncSetAttribute(tbs_search_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
-  CUDA_TRY(cudaFuncSetAttribute(row_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024));
-  int per_sm = 0;
-  CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tbs_search_kernel, kSearchThreads, smem_bytes));
-  int dev = 0, sms = 0;
-  CUDA_TRY(cudaGetDevice(&dev));
-  CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  return std::max(per_sm, 1) * sms;
 }
 
 int ensure_search_smem(size_t search_smem, size_t prep_smem) {

@@ -84,19 +84,14 @@ constexpr uint32_t kParentChunk = 1024;
 constexpr uint32_t kTaskItems = 128;
 
 // Device workspace of one search slot (one in-flight request).
-// A child found by the lookup phase of expansion: child node and
-// (parent index within the chunk << 16 | proposal column in the sorted row).
-struct Hit {
-  uint32_t child;
-  uint32_t qm;
-};
-
+//   pool_cap = beam_cap + 2 * beam_cap * max_topk: a step appends at most
+//   (its beams) * K pool entries, so the pool is trimmed to the final beam
+//   width only when the next step could overflow it.
 struct SlotView {
-  Hit *hits;         // [cand_cap]
-  Cand *next;        // [cand_cap]
-  Cand *pool;        // [pool_cap]
-  Cand *pool_tmp;    // [beam_cap]
-  Beam *beams[2];    // [beam_cap] each
+  Cand *next;        // [cand_cap]: this step's candidates
+  Cand *pool;        // [pool_cap]: result pool (entries that end a key)
+  Cand *pool_tmp;    // [beam_cap]: survivors of a pool trim
+  Beam *beams[2];    // [beam_cap] each; in-link beams from the front, branching from the back
   Hist *hist;        // [(max_outpos + 1) * beam_cap]
 };
 
@@ -156,9 +151,6 @@ int max_search_clusters(int cluster_size, size_t smem_bytes);
 // Team size for a batch of n requests: the largest power of two <= 16 with
 // n teams fitting on the device (FT_CLUSTER_SIZE overrides).
 int pick_cluster_size(uint32_t n, size_t smem_bytes, int *max_teams);
-
-// Configures kernel attributes once per device; returns max resident search CTAs.
-int configure_search_kernel(size_t smem_bytes);
 
 // Raises (never lowers) the dynamic shared-memory limits of the search and
 // row-prep kernels on the current device; returns max resident search CTAs

@@ -43,11 +43,10 @@ Engine::Engine(std::shared_ptr<DeviceTrie> trie, const EngineLimits &lim) : trie
   n_slots_ = (uint32_t)std::min<uint64_t>(lim.max_batch, (uint64_t)max_ctas_);
 
   const uint64_t B = lim.max_out_beams, K = lim.max_topk, L = lim.max_outpos, NB = lim.max_batch;
-  const uint64_t cand_cap = B * K, pool_cap = B + B * K;
+  const uint64_t cand_cap = B * K, pool_cap = B + 2 * B * K;
   try {
     std::vector<SlotView> slots(n_slots_);
     for (uint32_t s = 0; s < n_slots_; ++s) {
-      slots[s].hits = (Hit *)dalloc(sizeof(Hit) * cand_cap);
       slots[s].next = (Cand *)dalloc(sizeof(Cand) * cand_cap);
       slots[s].pool = (Cand *)dalloc(sizeof(Cand) * pool_cap);
       slots[s].pool_tmp = (Cand *)dalloc(sizeof(Cand) * B);
@@ -127,7 +126,7 @@ void Engine::fill_params(SearchParams &sp, const ft_search_params &prm, uint32_t
   sp.row_orig = d_row_orig_;
   sp.slots = d_slots_;
   sp.cand_cap = lim_.max_out_beams * lim_.max_topk;
-  sp.pool_cap = lim_.max_out_beams + lim_.max_out_beams * lim_.max_topk;
+  sp.pool_cap = lim_.max_out_beams + 2 * lim_.max_out_beams * lim_.max_topk;
   sp.beam_cap = (uint32_t)lim_.max_out_beams;
   sp.n_req = n_req;
   sp.n_slots = n_slots_;
