@@ -143,6 +143,8 @@ __device__ __forceinline__ Hist ld_hist(const Hist *p) {
 }
 
 // ---------------------------------------------------------- team state
+constexpr int kSuperBins = kRadixBins / 32;  // 64 super-bins of 32 radix bins
+constexpr uint32_t kMaxTeam = 16;            // CTAs per team (non-portable cluster size)
 // Counters of one step.  Two sets alternate by step parity: the set of step
 // t is read by every CTA after the barrier that closes step t, so the leader
 // clears it again only after the next step's expansion barrier.
@@ -168,16 +170,20 @@ struct alignas(16) TeamState {
   uint32_t eq_taken_trim;
   uint32_t pad;
   unsigned long long removed;     // pool entries dropped by trims so far
-  uint32_t hist[3][kRadixBins];   // merged radix histograms, by pass mod 3
   unsigned long long t_exp, t_sel, t_ovh, t_start;
 };
 
 // Per-CTA state; every CTA of a team derives the same values.
+// The radix histograms are double-buffered by pass parity: every CTA reads
+// every other CTA's histogram of a pass after that pass's barrier, and a
+// buffer is rewritten two passes later, after the next barrier.
 struct alignas(16) LocalState {
-  uint32_t hist[kRadixBins];
+  uint32_t hist[2][kRadixBins];
+  uint32_t super[2][kSuperBins];
+  uint32_t part[kMaxTeam * kSuperBins];  // per-rank super-bins / bins of a pass
+  uint32_t sel_sb, sel_above;
   uint32_t warp_sums[kWarps];
   uint32_t n_tasks;
-  uint32_t sel_digit, sel_above, sel_count;
   uint32_t n_in, n_br, n_next, pool_end;
   uint32_t key_min, key_max, pool_key_min, pool_key_max;
   unsigned long long pushes;
@@ -216,11 +222,22 @@ struct Ctx {
   double f_next;   // length-norm factor of the candidates' depth (t + 1)
   uint32_t rank;   // CTA rank in the team
   uint32_t cs;     // team size (CTAs)
+  // Ranges of this thread's pushes (top 32 bits of the first key word),
+  // folded into the team's at the end of expansion.
+  mutable uint32_t kmin, kmax, pkmin, pkmax;
   __device__ uint32_t gtid() const { return rank * blockDim.x + threadIdx.x; }
   __device__ uint32_t gthreads() const { return cs * blockDim.x; }
 };
 
-__device__ __forceinline__ void team_sync() { cg::this_cluster().sync(); }
+// Team barrier: a hardware cluster barrier (release/acquire at cluster
+// scope), or a CTA barrier for a one-CTA team (about 10x cheaper).
+__device__ __forceinline__ void team_sync(uint32_t cs) {
+  if (cs > 1) {
+    cg::this_cluster().sync();
+  } else {
+    __syncthreads();
+  }
+}
 
 // Records the first failed self-check (one writer wins).
 __device__ void report(const Ctx &c, uint32_t code, uint32_t n, uint32_t k, uint32_t got) {
@@ -266,14 +283,25 @@ __device__ __forceinline__ uint32_t append_slot(uint32_t *counter) {
   return base + g.thread_rank();
 }
 
-// Folds this thread's value into a team-wide [min, max] of u32.
-__device__ __forceinline__ void track_range(uint32_t *mn, uint32_t *mx, uint32_t v) {
-  cg::coalesced_group g = cg::coalesced_threads();
-  const uint32_t lo = cg::reduce(g, v, cg::less<uint32_t>());
-  const uint32_t hi = cg::reduce(g, v, cg::greater<uint32_t>());
-  if (g.thread_rank() == 0) {
-    atomicMin(mn, lo);
-    atomicMax(mx, hi);
+// Folds the key ranges of a warp's pushes into the team's (lane 0 issues one
+// remote atomic per bound).
+__device__ __forceinline__ void publish_ranges(const Ctx &c) {
+  uint32_t a = c.kmin, b = c.kmax, d = c.pkmin, e = c.pkmax;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a = min(a, __shfl_xor_sync(0xFFFFFFFFu, a, o));
+    b = max(b, __shfl_xor_sync(0xFFFFFFFFu, b, o));
+    d = min(d, __shfl_xor_sync(0xFFFFFFFFu, d, o));
+    e = max(e, __shfl_xor_sync(0xFFFFFFFFu, e, o));
+  }
+  const uint32_t lane = threadIdx.x & 31;
+  if (a <= b) {
+    if (lane == 0) atomicMin(&c.cnt->key_min, a);
+    if (lane == 1) atomicMax(&c.cnt->key_max, b);
+  }
+  if (d <= e) {
+    if (lane == 2) atomicMin(&c.T->pool_key_min, d);
+    if (lane == 3) atomicMax(&c.T->pool_key_max, e);
   }
 }
 
@@ -281,7 +309,9 @@ __device__ __forceinline__ void push_next(const Ctx &c, double score, uint32_t n
                                           uint32_t token) {
   // The range of the first key word lets the selection skip the bits every
   // candidate shares.
-  track_range(&c.cnt->key_min, &c.cnt->key_max, (uint32_t)(orderable(score * c.f_next) >> 32));
+  const uint32_t k32 = (uint32_t)(orderable(score * c.f_next) >> 32);
+  c.kmin = min(c.kmin, k32);
+  c.kmax = max(c.kmax, k32);
   const uint32_t i = append_slot(&c.cnt->n_next);
   if (i < c.p->cand_cap) {
     Cand v;
@@ -298,7 +328,9 @@ __device__ __forceinline__ void push_next(const Ctx &c, double score, uint32_t n
 
 __device__ __forceinline__ void push_pool(const Ctx &c, double score, uint32_t node, uint32_t parent,
                                           uint32_t token) {
-  track_range(&c.T->pool_key_min, &c.T->pool_key_max, (uint32_t)(orderable(score * c.f_next) >> 32));
+  const uint32_t k32 = (uint32_t)(orderable(score * c.f_next) >> 32);
+  c.pkmin = min(c.pkmin, k32);
+  c.pkmax = max(c.pkmax, k32);
   const uint32_t i = append_slot(&c.T->pool_end);
   if (i < c.p->pool_cap) {
     Cand v;
@@ -645,22 +677,25 @@ __device__ void expand_branch(const Ctx &c, const BranchTable &bt) {
 
 // ------------------------------------------------------------- selection
 // Exact top-k threshold over n candidates by the 192-bit key, computed by the
-// whole team with one cluster barrier per radix pass.  Each CTA histograms its
-// share of the keys that match the current prefix and adds the non-zero bins
-// into rank 0's merged histogram of this pass (buffer pass % 3); after the
-// barrier every CTA reads the merged histogram and derives the same digit.
-// While a pass fills its buffer, rank 0 zeroes the next pass's buffer, which
-// was last read before the previous barrier.  `start` leading bits of the
-// first key word are common to all n keys (equal to those of common_hi << 32).
-// On return every CTA's LocalState holds the threshold: with sel_ge every key
-// >= sel_prefix is taken (exactly k of them), otherwise keys > sel_prefix plus
-// sel_rem keys equal to it.
+// whole team with one cluster barrier per radix pass.  Each CTA histograms
+// its share of the keys that match the current prefix into its own shared
+// memory (2048 bins, buffer pass % 2) and sums them into 64 super-bins.  After
+// the barrier every CTA derives the same digit from the team's histograms:
+// warp r reads rank r's super-bins (one DSMEM load per lane, all ranks in
+// parallel), warp 0 sums and scans them; then the same for the 32 bins of the
+// super-bin that holds the rem-th key.  Nothing is merged with atomics.
+// `start` leading bits of the first key word are common to all n keys (equal
+// to those of common_hi << 32).  On return every CTA's LocalState holds the
+// threshold: with sel_ge every key >= sel_prefix is taken (exactly k of them),
+// otherwise keys > sel_prefix plus sel_rem keys equal to it.
 template <bool kPoolKeys>
 __device__ void team_radix_select(const Ctx &c, const Cand *v, uint32_t n, uint32_t k, uint32_t depth_const,
                                   int start, uint32_t common_hi) {
-  TeamState *T = c.T;
   LocalState *S = c.S;
+  const uint32_t cs = c.cs;
   const double *factor = c.p->factor;
+  cg::cluster_group cluster = cg::this_cluster();
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __syncthreads();  // this CTA may still be testing keys against the previous threshold
   if (threadIdx.x == 0) {
     const uint64_t m0 = start >= 32 ? 0xFFFFFFFF00000000ull : (start == 0 ? 0ull : ~0ull << (64 - start));
@@ -670,66 +705,113 @@ __device__ void team_radix_select(const Ctx &c, const Cand *v, uint32_t n, uint3
     S->sel_ge = 0;
   }
   __syncthreads();
+  const uint32_t max_depth = c.step + 1;
+  const double fac_const = factor[depth_const];
   for (int from_top = start; from_top < kKeyBits; from_top += kRadixBits) {
     const int width = min(kRadixBits, kKeyBits - from_top);
-    const uint32_t buf = S->pass % 3;
-    for (int b = threadIdx.x; b < kRadixBins; b += blockDim.x) S->hist[b] = 0;
+    const uint32_t buf = S->pass & 1u;
+    uint32_t *hist = S->hist[buf];
+    uint32_t *super = S->super[buf];
+    for (int b = threadIdx.x; b < kRadixBins; b += blockDim.x) hist[b] = 0;
     const Key3 P = S->sel_prefix, M = S->sel_mask;
     __syncthreads();
     for (uint32_t i = c.gtid(); i < n; i += c.gthreads()) {
       const Cand cv = ld_cand(v + i);
-      const uint32_t depth = kPoolKeys ? min(cv.aux, c.step + 1) : depth_const;
-      const Key3 key = cand_key(cv, factor[depth], depth);
+      const uint32_t depth = kPoolKeys ? min(cv.aux, max_depth) : depth_const;
+      const Key3 key = cand_key(cv, kPoolKeys ? factor[depth] : fac_const, depth);
       if ((key.w[0] & M.w[0]) == P.w[0] && (key.w[1] & M.w[1]) == P.w[1] && (key.w[2] & M.w[2]) == P.w[2])
-        atomicAdd(&S->hist[key_bits(key, from_top, width)], 1u);
+        atomicAdd(&hist[key_bits(key, from_top, width)], 1u);
     }
     __syncthreads();
-    if (c.cs > 1) {
-      for (int b = threadIdx.x; b < kRadixBins; b += blockDim.x)
-        if (S->hist[b]) atomicAdd(&T->hist[buf][b], S->hist[b]);
-      if (c.rank == 0) {
-        uint32_t *nb = T->hist[(buf + 1) % 3];
-        for (int b = threadIdx.x; b < kRadixBins; b += blockDim.x) nb[b] = 0;
-      }
+    {
+      // Super-bin sums: thread i sums bins 4i..4i+3; 8 lanes make a super-bin.
+      const uint4 q = *reinterpret_cast<const uint4 *>(hist + 4 * threadIdx.x);
+      uint32_t s4 = q.x + q.y + q.z + q.w;
+      s4 += __shfl_xor_sync(0xFFFFFFFFu, s4, 1);
+      s4 += __shfl_xor_sync(0xFFFFFFFFu, s4, 2);
+      s4 += __shfl_xor_sync(0xFFFFFFFFu, s4, 4);
+      if ((threadIdx.x & 7) == 0) super[threadIdx.x >> 3] = s4;
     }
-    team_sync();
-    // Bins from the top: thread i owns bins 2047-4i .. 2044-4i.
-    constexpr int kPer = kRadixBins / kSearchThreads;
-    static_assert(kPer == 4, "one uint4 of bins per thread");
-    const uint32_t *H = c.cs > 1 ? T->hist[buf] : S->hist;
-    const uint4 q4 = *reinterpret_cast<const uint4 *>(H + kRadixBins - kPer * (threadIdx.x + 1));
-    const uint32_t mine[kPer] = {q4.w, q4.z, q4.y, q4.x};
-    const uint32_t sum = mine[0] + mine[1] + mine[2] + mine[3];
-    const uint32_t rem = S->sel_rem;
-    const uint32_t above = block_exclusive_sum(sum, S);
-    if (above < rem && rem <= above + sum) {
-      uint32_t acc = above;
+    team_sync(cs);
+    uint32_t *part = S->part;
+    if (warp < cs) {
+      const uint2 pv = *reinterpret_cast<const uint2 *>(cluster.map_shared_rank(super, warp) + 2 * lane);
+      *reinterpret_cast<uint2 *>(part + warp * kSuperBins + 2 * lane) = pv;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      const uint32_t rem = S->sel_rem;
+      // Lane l holds super-bins 63-2l (upper) and 62-2l (lower).
+      uint32_t hi_s = 0, lo_s = 0;
+      for (uint32_t r = 0; r < cs; ++r) {
+        const uint2 pv = *reinterpret_cast<const uint2 *>(part + r * kSuperBins + kSuperBins - 2 - 2 * lane);
+        hi_s += pv.y;
+        lo_s += pv.x;
+      }
+      uint32_t inc = hi_s + lo_s;
 #pragma unroll
-      for (int q = 0; q < kPer; ++q) {
-        if (acc + mine[q] >= rem) {
-          S->sel_digit = kRadixBins - 1 - kPer * threadIdx.x - q;
-          S->sel_above = acc;
-          S->sel_count = mine[q];
-          break;
-        }
-        acc += mine[q];
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+        if (lane >= (uint32_t)o) inc += y;
+      }
+      const uint32_t excl = inc - hi_s - lo_s;
+      const uint32_t total = __shfl_sync(0xFFFFFFFFu, inc, 31);
+      const uint32_t who = __ffs(__ballot_sync(0xFFFFFFFFu, excl < rem && rem <= inc));  // 1-based, 0 if none
+      uint32_t sb = 0xFFFFFFFFu, sb_above = 0;
+      if (who != 0 && total >= rem) {
+        const uint32_t w = who - 1;
+        const uint32_t e = __shfl_sync(0xFFFFFFFFu, excl, w);
+        const uint32_t h = __shfl_sync(0xFFFFFFFFu, hi_s, w);
+        const bool upper = rem <= e + h;
+        sb = upper ? kSuperBins - 1 - 2 * w : kSuperBins - 2 - 2 * w;
+        sb_above = upper ? e : e + h;
+      }
+      if (lane == 0) {
+        S->sel_sb = sb;
+        S->sel_above = sb_above;
       }
     }
-    if (threadIdx.x == blockDim.x - 1 && above + sum < rem) S->sel_digit = 0xFFFFFFFFu;
     __syncthreads();
-    if (threadIdx.x == 0) {
-      S->pass += 1;
-      if (S->sel_digit == 0xFFFFFFFFu) {
-        // Fewer keys match the prefix than remain to be taken: the key range
-        // was wrong.  Report it and take everything at or above the prefix.
-        atomicOr(c.p->status, kStatusSelection);
-        S->sel_ge = 1;
-      } else {
-        const uint32_t d = S->sel_digit;
-        S->sel_rem = rem - S->sel_above;
-        key_set_bits(S->sel_prefix, from_top, width, d);
-        key_set_bits(S->sel_mask, from_top, width, low_mask(width));
-        if (S->sel_count == S->sel_rem) S->sel_ge = 1;
+    const uint32_t sb = S->sel_sb;
+    if (sb != 0xFFFFFFFFu && warp < cs) part[warp * 32 + lane] = cluster.map_shared_rank(hist, warp)[sb * 32 + 31 - lane];
+    __syncthreads();
+    if (warp == 0) {
+      const uint32_t rem = S->sel_rem;
+      uint32_t digit = 0xFFFFFFFFu, above = 0, count = 0;
+      if (sb != 0xFFFFFFFFu) {
+        // Lane l holds bin sb*32 + 31 - l (descending).
+        uint32_t bv = 0;
+        for (uint32_t r = 0; r < cs; ++r) bv += part[r * 32 + lane];
+        uint32_t binc = bv;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, binc, o);
+          if (lane >= (uint32_t)o) binc += y;
+        }
+        const uint32_t bexcl = binc - bv;
+        const uint32_t sb_above = S->sel_above;
+        const uint32_t need = rem - sb_above;
+        const uint32_t who2 = __ffs(__ballot_sync(0xFFFFFFFFu, bexcl < need && need <= binc));
+        if (who2 != 0) {
+          const uint32_t w2 = who2 - 1;
+          digit = sb * 32 + 31 - w2;
+          above = sb_above + __shfl_sync(0xFFFFFFFFu, bexcl, w2);
+          count = __shfl_sync(0xFFFFFFFFu, bv, w2);
+        }
+      }
+      if (lane == 0) {
+        S->pass += 1;
+        if (digit == 0xFFFFFFFFu) {
+          // Fewer keys match the prefix than remain to be taken: the key range
+          // was wrong.  Report it and take everything at or above the prefix.
+          atomicOr(c.p->status, kStatusSelection);
+          S->sel_ge = 1;
+        } else {
+          S->sel_rem = rem - above;
+          key_set_bits(S->sel_prefix, from_top, width, digit);
+          key_set_bits(S->sel_mask, from_top, width, low_mask(width));
+          if (count == S->sel_rem) S->sel_ge = 1;
+        }
       }
     }
     __syncthreads();
@@ -928,8 +1010,6 @@ __device__ void search_request(const SearchParams &p, uint32_t req, const SlotVi
     T->eq_taken_trim = 0;
     T->removed = 0;
   }
-  if (rank == 0)
-    for (int b = threadIdx.x; b < 3 * kRadixBins; b += blockDim.x) (&T->hist[0][0])[b] = 0;
   if (threadIdx.x == 0) S->pass = 0;
   RowView row;
   row.id = reinterpret_cast<uint32_t *>(dyn);
@@ -943,7 +1023,7 @@ __device__ void search_request(const SearchParams &p, uint32_t req, const SlotVi
     bt.score = reinterpret_cast<double *>(tb + sizeof(uint4) * kParentChunk);
     bt.start = reinterpret_cast<uint32_t *>(tb + (sizeof(uint4) + sizeof(double)) * kParentChunk);
   }
-  team_sync();
+  team_sync(cs);
 
   Ctx c;
   c.p = &p;
@@ -1002,9 +1082,12 @@ __device__ void search_request(const SearchParams &p, uint32_t req, const SlotVi
 
     c.cur = slot.beams[par];
     c.f_next = p.factor[t + 1];
+    c.kmin = c.pkmin = 0xFFFFFFFFu;
+    c.kmax = c.pkmax = 0;
     expand_inlink(c);
     expand_branch(c, bt);
-    team_sync();
+    publish_ranges(c);
+    team_sync(cs);
     unsigned long long t2 = 0;
     if (leader) t2 = global_ns();
 
@@ -1038,7 +1121,7 @@ __device__ void search_request(const SearchParams &p, uint32_t req, const SlotVi
       }
       trimmed = true;
     }
-    team_sync();
+    team_sync(cs);
     if (leader) {
       const unsigned long long t3 = global_ns();
       T->t_ovh += t1 - t0;
@@ -1048,7 +1131,7 @@ __device__ void search_request(const SearchParams &p, uint32_t req, const SlotVi
   }
   // The pool survivors copied back at the last step start must land before
   // the final trim reads the pool.
-  team_sync();
+  team_sync(cs);
   const unsigned long long t4 = leader ? global_ns() : 0ull;
   if (threadIdx.x == 0) {
     S->pool_end = min(T->pool_end, (uint32_t)p.pool_cap);
@@ -1067,7 +1150,7 @@ __device__ void search_request(const SearchParams &p, uint32_t req, const SlotVi
   if (n_pool > final_beam) {
     c.step = L - 1;  // pool depths are at most L
     trim_pool(c, n_pool, final_beam);
-    team_sync();
+    team_sync(cs);
     out_pool = slot.pool_tmp;
     n_out = final_beam;
     if (threadIdx.x == 0) S->n_next = T->n_compact;
@@ -1103,7 +1186,7 @@ __global__ void __launch_bounds__(kSearchThreads, 1) tbs_search_kernel(const Sea
   const SlotView slot = p.slots[team];
   for (uint32_t req = team; req < p.n_req; req += n_teams) {
     search_request(p, req, slot, T, &local_state, rank, cs, dyn);
-    team_sync();  // rank 0's state is reused by the next request
+    team_sync(cs);  // rank 0's state is reused by the next request
   }
 }
 
