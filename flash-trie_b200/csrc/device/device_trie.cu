@@ -1,6 +1,7 @@
 #include <cuda_runtime.h>
 #include <omp.h>
 
+#include <algorithm>
 #include <cstring>
 #include <string>
 
@@ -149,6 +150,20 @@ void build_hash_index(HostDeviceImage &out, int num_threads) {
   }
 }
 
+void pack_node_records(const HostDeviceImage &img, std::vector<uint32_t> &out, int num_threads) {
+  const uint64_t N = img.num_nodes;
+  out.assign(4 * N, 0);
+#pragma omp parallel for schedule(static) num_threads(num_threads)
+  for (int64_t n = 0; n < (int64_t)N; ++n) {
+    const uint32_t c0 = img.child_begin[n], d = img.child_begin[n + 1] - c0;
+    uint32_t *r = out.data() + 4 * n;
+    r[0] = img.first_label[n];
+    r[1] = img.link_off[n];
+    r[2] = c0;
+    r[3] = ((uint32_t)img.flags[n] << 24) | std::min(d, kFanoutMask);
+  }
+}
+
 DeviceTrie::~DeviceTrie() { release(); }
 
 void DeviceTrie::release() {
@@ -156,17 +171,13 @@ void DeviceTrie::release() {
     int prev = -1;
     cudaGetDevice(&prev);
     cudaSetDevice(device);
-    cudaFree(child_begin);
-    cudaFree(first_label);
-    cudaFree(link_off);
-    cudaFree(flags);
+    cudaFree(node);
     cudaFree(tail);
     cudaFree(tail_end);
     cudaFree(hash);
     if (prev >= 0) cudaSetDevice(prev);
   }
-  child_begin = first_label = link_off = tail = nullptr;
-  flags = nullptr;
+  node = tail = nullptr;
   tail_end = nullptr;
   hash = nullptr;
   hash_slots = 0;
@@ -194,10 +205,11 @@ void DeviceTrie::upload(const LoudsLevel &lv, int num_threads) {
   tail_size = lv.tail.size();
   binary_tail = img.binary_tail;
   try {
-    child_begin = upload_array(img.child_begin.data(), img.child_begin.size(), bytes);
-    first_label = upload_array(img.first_label.data(), img.first_label.size(), bytes);
-    link_off = upload_array(img.link_off.data(), img.link_off.size(), bytes);
-    flags = upload_array(img.flags.data(), img.flags.size(), bytes);
+    {
+      std::vector<uint32_t> rec;
+      pack_node_records(img, rec, num_threads);
+      node = upload_array(rec.data(), rec.size(), bytes);
+    }
     tail = upload_array(lv.tail.data(), lv.tail.size(), bytes);
     if (binary_tail) tail_end = upload_array(lv.tail_end_flags.units.data(), lv.tail_end_flags.units.size(), bytes);
     hash = upload_array(img.hash.data(), img.hash.size(), bytes);

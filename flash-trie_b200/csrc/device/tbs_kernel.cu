@@ -117,25 +117,32 @@ __device__ __forceinline__ void key_set_bits(Key3 &k, int from_top, int width, u
 // the team and read by another after a cluster barrier; they are loaded
 // through L2 (ld.global.cg) so that no SM can see a line it cached earlier.
 __device__ __forceinline__ Cand ld_cand(const Cand *p) {
+  const uint4 a = __ldcg(reinterpret_cast<const uint4 *>(p));
+  const uint4 b = __ldcg(reinterpret_cast<const uint4 *>(p) + 1);
   Cand c;
-  c.score = __ldcg(&p->score);
-  const uint2 a = __ldcg(reinterpret_cast<const uint2 *>(&p->node));
-  const uint2 b = __ldcg(reinterpret_cast<const uint2 *>(&p->parent));
-  c.node = a.x;
-  c.aux = a.y;
+  c.score = __hiloint2double((int)a.y, (int)a.x);
+  c.node = a.z;
+  c.aux = a.w;
   c.parent = b.x;
   c.token = b.y;
+  c.c0 = b.z;
+  c.dw = b.w;
   return c;
 }
 
 __device__ __forceinline__ Beam ld_beam(const Beam *p) {
-  Beam b;
-  b.score = __ldcg(&p->score);
-  const uint2 a = __ldcg(reinterpret_cast<const uint2 *>(&p->node));
-  b.node = a.x;
-  b.off = a.y;
-  return b;
+  const uint2 *q = reinterpret_cast<const uint2 *>(p);
+  const uint2 a = __ldcg(q), b = __ldcg(q + 1), d = __ldcg(q + 2);
+  Beam r;
+  r.score = __hiloint2double((int)a.y, (int)a.x);
+  r.node = b.x;
+  r.off = b.y;
+  r.c0 = d.x;
+  r.dw = d.y;
+  return r;
 }
+
+__device__ __forceinline__ uint32_t rec_flags(uint32_t dw) { return dw >> 24; }
 
 __device__ __forceinline__ Hist ld_hist(const Hist *p) {
   const uint2 a = __ldcg(reinterpret_cast<const uint2 *>(p));
@@ -306,7 +313,7 @@ __device__ __forceinline__ void publish_ranges(const Ctx &c) {
 }
 
 __device__ __forceinline__ void push_next(const Ctx &c, double score, uint32_t node, uint32_t off, uint32_t parent,
-                                          uint32_t token) {
+                                          uint32_t token, uint32_t c0, uint32_t dw) {
   // The range of the first key word lets the selection skip the bits every
   // candidate shares.
   const uint32_t k32 = (uint32_t)(orderable(score * c.f_next) >> 32);
@@ -320,6 +327,8 @@ __device__ __forceinline__ void push_next(const Ctx &c, double score, uint32_t n
     v.aux = off;
     v.parent = parent;
     v.token = token;
+    v.c0 = c0;
+    v.dw = dw;
     c.slot.next[i] = v;
   } else {
     atomicOr(c.p->status, kStatusCandOverflow);
@@ -339,6 +348,8 @@ __device__ __forceinline__ void push_pool(const Ctx &c, double score, uint32_t n
     v.aux = c.step + 1;  // depth
     v.parent = parent;
     v.token = token;
+    v.c0 = 0;
+    v.dw = 0;
     c.slot.pool[i] = v;
   } else {
     atomicOr(c.p->status, kStatusPoolOverflow);
@@ -416,9 +427,9 @@ __device__ void expand_inlink(const Ctx &c) {
       if (lp <= tt || b.score + lp <= st) continue;
       const double score = b.score + lp;
       if (end) {
-        if (__ldg(t.flags + b.node) & kNodeFlagTerminal) push_pool(c, score, b.node, i, tok);
+        if (rec_flags(b.dw) & kNodeFlagTerminal) push_pool(c, score, b.node, i, tok);
       } else {
-        push_next(c, score, b.node, off + 1, i, tok);
+        push_next(c, score, b.node, off + 1, i, tok, b.c0, b.dw);
       }
     }
   }
@@ -432,64 +443,59 @@ constexpr uint32_t kItemsPerLane = kTaskItems / 32;
 
 // The shorter side is iterated; a large fan-out uses the node's hash table
 // (one probe per proposal), or a binary search when it has none.
-__device__ __forceinline__ uint32_t pick_mode(uint32_t d, uint32_t K, uint8_t f) {
+__device__ __forceinline__ uint32_t pick_mode(uint32_t d, uint32_t K, uint32_t f) {
   if (d <= 2u * K + 32u) return kModeScan;
   if (f & kNodeFlagHashed) return kModeHash;
   return kModeBin;
 }
 
-// A child `child` (flags f, link offset lo) of a branching parent matched
-// sorted-row column m: the candidate and pool entry it yields
-// (tbs-kernels.cu:295-317).
+// A child `child` (node record r) of a branching parent matched sorted-row
+// column m: the candidate and pool entry it yields (tbs-kernels.cu:295-317).
 __device__ __forceinline__ void emit_child(const Ctx &c, double pscore, uint32_t parent_idx, uint32_t child,
-                                           uint8_t f, uint32_t lo, uint32_t m) {
+                                           const uint4 &r, uint32_t m) {
   const double lp = (double)c.row.lp[m];
   if (lp <= c.p->token_threshold || pscore + lp <= c.p->sent_threshold) return;
   const double score = pscore + lp;
   const uint32_t token = c.row.id[m];
+  const uint32_t f = rec_flags(r.w);
   if (!(f & kNodeFlagLink)) {
-    push_next(c, score, child, kNoOffset, parent_idx, token);
+    push_next(c, score, child, r.y, parent_idx, token, r.z, r.w);
     if (f & kNodeFlagTerminal) push_pool(c, score, child, parent_idx, token);
   } else if (f & kNodeFlagLinkEnds1) {
     // The link's string ended with its first token (tbs-kernels.cu:310-313).
     if (f & kNodeFlagTerminal) push_pool(c, score, child, parent_idx, token);
   } else {
-    push_next(c, score, child, lo + 1, parent_idx, token);
+    push_next(c, score, child, r.y + 1, parent_idx, token, r.z, r.w);
   }
 }
 
-// Lookup tasks: a lane's four items issue each round of loads (labels or
-// probes, then the found children's flags and link offsets) before using any.
+// Lookup tasks: a lane's four items issue each round of loads (records,
+// probes) before using any.
 __device__ __forceinline__ void task_scan(const Ctx &c, uint32_t c0, uint32_t d, uint32_t first_item, double score,
                                           uint32_t parent_idx) {
   const TrieView &t = c.p->trie;
   const uint32_t lane = threadIdx.x & 31;
-  uint32_t lab[kItemsPerLane], mlo[kItemsPerLane], lo[kItemsPerLane];
-  uint8_t f[kItemsPerLane];
+  uint4 rec[kItemsPerLane];
+  uint32_t mlo[kItemsPerLane];
 #pragma unroll
   for (uint32_t k = 0; k < kItemsPerLane; ++k) {
     const uint32_t i = first_item + 32u * k + lane;
-    lab[k] = i < d ? __ldg(t.first_label + c0 + i) : 0u;
+    rec[k] = i < d ? __ldg(t.node + c0 + i) : make_uint4(0, 0, 0, 0);
   }
 #pragma unroll
   for (uint32_t k = 0; k < kItemsPerLane; ++k) {
     const uint32_t i = first_item + 32u * k + lane;
     mlo[k] = c.row.K;
     if (i < d) {
-      const uint32_t m = row_lower_bound(c.row, lab[k]);
-      if (m < c.row.K && c.row.id[m] == lab[k]) mlo[k] = m;
-    }
-    if (mlo[k] < c.row.K) {
-      f[k] = __ldg(t.flags + c0 + i);
-      lo[k] = __ldg(t.link_off + c0 + i);
+      const uint32_t m = row_lower_bound(c.row, rec[k].x);
+      if (m < c.row.K && c.row.id[m] == rec[k].x) mlo[k] = m;
     }
   }
 #pragma unroll
   for (uint32_t k = 0; k < kItemsPerLane; ++k) {
-    if (mlo[k] >= c.row.K) continue;
     const uint32_t child = c0 + first_item + 32u * k + lane;
-    for (uint32_t m = mlo[k]; m < c.row.K && c.row.id[m] == lab[k]; ++m)
-      emit_child(c, score, parent_idx, child, f[k], lo[k], m);
+    for (uint32_t m = mlo[k]; m < c.row.K && c.row.id[m] == rec[k].x; ++m)
+      emit_child(c, score, parent_idx, child, rec[k], m);
   }
 }
 
@@ -499,8 +505,8 @@ __device__ __forceinline__ void task_hash(const Ctx &c, uint32_t base, uint32_t 
   const double tt = c.p->token_threshold, st = c.p->sent_threshold;
   const uint32_t lane = threadIdx.x & 31;
   const uint32_t mask = (1u << lg) - 1u;
-  uint32_t x[kItemsPerLane], h[kItemsPerLane], child[kItemsPerLane], lo[kItemsPerLane];
-  uint8_t f[kItemsPerLane];
+  uint32_t x[kItemsPerLane], h[kItemsPerLane], child[kItemsPerLane];
+  uint4 rec[kItemsPerLane];
   uint2 slot[kItemsPerLane];
   bool on[kItemsPerLane];
 #pragma unroll
@@ -530,14 +536,11 @@ __device__ __forceinline__ void task_hash(const Ctx &c, uint32_t base, uint32_t 
       sl = __ldg(t.hash + base + hk);
     }
     child[k] = sl.y;
-    if (child[k] != 0) {
-      f[k] = __ldg(t.flags + child[k]);
-      lo[k] = __ldg(t.link_off + child[k]);
-    }
+    if (child[k] != 0) rec[k] = __ldg(t.node + child[k]);
   }
 #pragma unroll
   for (uint32_t k = 0; k < kItemsPerLane; ++k)
-    if (child[k] != 0) emit_child(c, score, parent_idx, child[k], f[k], lo[k], first_item + 32u * k + lane);
+    if (child[k] != 0) emit_child(c, score, parent_idx, child[k], rec[k], first_item + 32u * k + lane);
 }
 
 __device__ __forceinline__ void task_bin(const Ctx &c, uint32_t c0, uint32_t d, uint32_t first_item, double score,
@@ -545,9 +548,10 @@ __device__ __forceinline__ void task_bin(const Ctx &c, uint32_t c0, uint32_t d, 
   const TrieView &t = c.p->trie;
   const double tt = c.p->token_threshold, st = c.p->sent_threshold;
   const uint32_t lane = threadIdx.x & 31;
-  const uint32_t *labs = t.first_label + c0;
-  uint32_t x[kItemsPerLane], pos[kItemsPerLane], lo[kItemsPerLane];
-  uint8_t f[kItemsPerLane];
+  // Labels are the first word of each 16-byte record.
+  const uint32_t *labs = reinterpret_cast<const uint32_t *>(t.node + c0);
+  uint32_t x[kItemsPerLane], pos[kItemsPerLane];
+  uint4 rec[kItemsPerLane];
   bool on[kItemsPerLane];
 #pragma unroll
   for (uint32_t k = 0; k < kItemsPerLane; ++k) {
@@ -567,7 +571,7 @@ __device__ __forceinline__ void task_bin(const Ctx &c, uint32_t c0, uint32_t d, 
     const uint32_t half = n >> 1;
     uint32_t v[kItemsPerLane];
 #pragma unroll
-    for (uint32_t k = 0; k < kItemsPerLane; ++k) v[k] = __ldg(labs + pos[k] + half - 1);
+    for (uint32_t k = 0; k < kItemsPerLane; ++k) v[k] = __ldg(labs + 4u * (pos[k] + half - 1));
 #pragma unroll
     for (uint32_t k = 0; k < kItemsPerLane; ++k) pos[k] = v[k] < x[k] ? pos[k] + half : pos[k];
     n -= half;
@@ -576,20 +580,20 @@ __device__ __forceinline__ void task_bin(const Ctx &c, uint32_t c0, uint32_t d, 
   for (uint32_t k = 0; k < kItemsPerLane; ++k) {
     if (on[k] && d > 0) {
       uint32_t p = pos[k];
-      if (__ldg(labs + p) < x[k]) ++p;
+      if (__ldg(labs + 4u * p) < x[k]) ++p;
       pos[k] = p;
-      on[k] = p < d && __ldg(labs + p) == x[k];
+      on[k] = p < d;
     } else {
       on[k] = false;
     }
     if (on[k]) {
-      f[k] = __ldg(t.flags + c0 + pos[k]);
-      lo[k] = __ldg(t.link_off + c0 + pos[k]);
+      rec[k] = __ldg(t.node + c0 + pos[k]);
+      on[k] = rec[k].x == x[k];
     }
   }
 #pragma unroll
   for (uint32_t k = 0; k < kItemsPerLane; ++k)
-    if (on[k]) emit_child(c, score, parent_idx, c0 + pos[k], f[k], lo[k], first_item + 32u * k + lane);
+    if (on[k]) emit_child(c, score, parent_idx, c0 + pos[k], rec[k], first_item + 32u * k + lane);
 }
 
 // Branching beams, per chunk of parents: every CTA builds the same task table
@@ -616,18 +620,22 @@ __device__ void expand_branch(const Ctx &c, const BranchTable &bt) {
       if ((uint64_t)b.node >= t.num_nodes) {
         atomicOr(c.p->status, kStatusNodeBounds);
       } else {
-        const uint32_t c0 = __ldg(t.child_begin + b.node);
-        const uint32_t c1 = __ldg(t.child_begin + b.node + 1);
-        const uint32_t d = c1 > c0 ? c1 - c0 : 0;
-        uint8_t f = 0;
-        uint32_t hbase = 0;
-        if (d > 2u * K + 32u) {
-          f = __ldg(t.flags + b.node);
-          if (f & kNodeFlagHashed) hbase = __ldg(t.link_off + b.node);
+        // The beam carries its node's child range and flags.
+        const uint32_t c0 = b.c0;
+        uint32_t d = b.dw & kFanoutMask;
+        if (d == kFanoutMask) {
+          const uint32_t end = (uint64_t)b.node + 1 < t.num_nodes ? __ldg(t.node + b.node + 1).z
+                                                                 : (uint32_t)t.num_nodes;
+          d = end > c0 ? end - c0 : 0;
         }
+        if ((uint64_t)c0 + d > t.num_nodes) {
+          atomicOr(c.p->status, kStatusNodeBounds);
+          d = 0;
+        }
+        const uint32_t f = rec_flags(b.dw);
         const uint32_t mode = pick_mode(d, K, f);
         const uint32_t items = (d == 0) ? 0u : (mode == kModeScan ? d : K);
-        info = make_uint4(c0, d, hbase, mode | ((uint32_t)(f >> 3) << 8));
+        info = make_uint4(c0, d, b.off, mode | ((f >> 3) << 8));
         my_tasks[r] = (items + kTaskItems - 1) / kTaskItems;
       }
       bt.info[q] = info;
@@ -853,7 +861,7 @@ __device__ void materialize_next(const Ctx &c, uint32_t n, uint32_t k, Beam *out
     // In-link beams fill the buffer from the front, branching beams from the
     // back; the capped total keeps the two from overlapping.
     uint32_t idx;
-    if (v.aux != kNoOffset) {
+    if (rec_flags(v.dw) & kNodeFlagLink) {
       idx = append_slot(&c.cnt->n_in_new);
     } else {
       idx = beam_cap - 1 - append_slot(&c.cnt->n_br_new);
@@ -862,6 +870,8 @@ __device__ void materialize_next(const Ctx &c, uint32_t n, uint32_t k, Beam *out
     b.score = v.score;
     b.node = v.node;
     b.off = v.aux;
+    b.c0 = v.c0;
+    b.dw = v.dw;
     out_beams[idx] = b;
     hist[idx] = Hist{v.parent, v.token};
   }
@@ -996,10 +1006,13 @@ __device__ void search_request(const SearchParams &p, uint32_t req, const SlotVi
   }
   const uint32_t beam_cap = p.beam_cap;
   if (leader) {
+    const uint4 r = __ldg(p.trie.node);  // the root (node 0) is never a link node
     Beam root;
     root.score = 0.0;
     root.node = 0;
-    root.off = kNoOffset;
+    root.off = r.y;
+    root.c0 = r.z;
+    root.dw = r.w;
     slot.beams[0][beam_cap - 1] = root;
     reset_counters(&T->cnt[0]);
     reset_counters(&T->cnt[1]);

@@ -10,28 +10,34 @@
 
 namespace ftb {
 
-constexpr uint32_t kNoOffset = 0xFFFFFFFFu;  // Beam::off of a beam not inside a link
 constexpr int kSearchThreads = 512;          // threads per search CTA
 constexpr int kRefBlock = 512;               // threads per CTA of the reference kernel
                                              // (tbs-kernels.cu:10): in-link matches are
                                              // taken first-per-residue-class of this size
 
-// Candidate produced by expansion (24 bytes).
-//   next-candidates: aux = tail offset of the next token (kNoOffset if none)
+// Candidate produced by expansion (32 bytes).
+//   next-candidates: aux = tail offset of the next token for a link node (an
+//                    in-link beam), the hash base for a hashed plain node;
+//                    c0 / dw = the node record's child range and flags, so
+//                    the next step needs no further load to expand it
 //   pool entries:    aux = depth
-struct Cand {
+struct alignas(16) Cand {
   double score;
   uint32_t node;
   uint32_t aux;
   uint32_t parent;  // index of the parent beam in the step's beam array
   uint32_t token;
+  uint32_t c0;
+  uint32_t dw;
 };
 
-// A live beam (16 bytes).
+// A live beam (24 bytes).  In-link iff its node is a link node.
 struct Beam {
   double score;
   uint32_t node;
-  uint32_t off;  // next tail cell for an in-link beam, kNoOffset otherwise
+  uint32_t off;  // next tail cell (in-link beam) or hash base (hashed plain node)
+  uint32_t c0;
+  uint32_t dw;
 };
 
 // History record of the beam at index i of step s: its parent's index at
@@ -50,10 +56,7 @@ struct ReqMeta {
 };
 
 struct TrieView {
-  const uint32_t *child_begin;
-  const uint32_t *first_label;
-  const uint32_t *link_off;
-  const uint8_t *flags;
+  const uint4 *node;
   const uint32_t *tail;
   const uint64_t *tail_end;  // nullptr for a text tail
   const uint2 *hash;         // per-node child tables {label, child}, see device_trie.hpp
@@ -64,10 +67,7 @@ struct TrieView {
 
 inline TrieView make_trie_view(const DeviceTrie &d) {
   TrieView v;
-  v.child_begin = d.child_begin;
-  v.first_label = d.first_label;
-  v.link_off = d.link_off;
-  v.flags = d.flags;
+  v.node = reinterpret_cast<const uint4 *>(d.node);
   v.tail = d.tail;
   v.tail_end = d.binary_tail ? d.tail_end : nullptr;
   v.hash = reinterpret_cast<const uint2 *>(d.hash);
