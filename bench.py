@@ -481,7 +481,7 @@ def run_b200(args, cfg):
             "phase_ms_per_request": dict(zip(["expansion", "validation(fused)", "selection", "overhead", "kernel"],
                                               (phase_sum / max(e2e_steps * nb, 1)).round(5).tolist())),
             "clocks": clk,
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": args.steps,
             "setup_s": {"trie_build": build_s, "init_tbs_gpu": init_s},
         }
         print(json.dumps(line))

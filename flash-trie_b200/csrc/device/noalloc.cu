@@ -8,8 +8,8 @@
 // milliseconds) is not acceptable.  Such callers upload the trie once at start-up
 // (ft_trie_init_tbs_gpu) and afterwards only pass input and output buffers.
 //
-// The search's scratch memory (candidates, result pool, beams, history, sorted
-// rows, request metadata and the status word) lives in the file-scope array
+// The search's scratch memory (candidates, result pool, beams, history,
+// request metadata and the status word) lives in the file-scope array
 // below: a fixed kNoAllocScratchBytes that every GPU which loads this library
 // keeps until the process exits.  Nothing here calls cudaMalloc, cudaFree or any
 // allocating routine.
@@ -55,7 +55,7 @@ inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 // Byte offsets of the scratch regions for one call.
 struct Layout {
-  size_t status, meta, factor, slots, rows_id, rows_lp, rows_orig, slot0, slot_bytes;
+  size_t status, meta, factor, slots, slot0, slot_bytes;
   size_t cand, pool, pool_tmp, beams0, beams1, hist;  // within a slot
   size_t total;
 };
@@ -71,13 +71,6 @@ Layout plan(uint32_t n, uint32_t L, uint32_t K, uint32_t B, uint32_t n_slots) {
   o = align256(o + 8ull * (L + 1));
   a.slots = o;
   o = align256(o + sizeof(ftb::SlotView) * n_slots);
-  const size_t rows = 4ull * n * L * K;
-  a.rows_id = o;
-  o = align256(o + rows);
-  a.rows_lp = o;
-  o = align256(o + rows);
-  a.rows_orig = o;
-  o = align256(o + rows);
   size_t s = 0;
   a.cand = s;
   s = align256(s + sizeof(ftb::Cand) * (size_t)B * K);
@@ -185,10 +178,8 @@ extern "C" int ft_tbs_batch_device_noalloc(ft_trie *trie, const ft_device_batch 
     FactorTable ft;
     std::memset(&ft, 0, sizeof(ft));
     for (uint32_t d = 0; d <= L; ++d) ft.f[d] = std::pow(6.0 / (5.0 + (double)d), prm->length_norm);
-    uint32_t P2 = 1;
-    while (P2 < std::max<uint32_t>(K, 1)) P2 <<= 1;
     const size_t smem = ftb::search_smem_bytes(K, B);
-    const int max_ctas = ftb::ensure_search_smem(smem, (size_t)P2 * 8);
+    const int max_ctas = ftb::ensure_search_smem(smem);
     noalloc_setup_kernel<<<1, 256, 0, stream>>>(a, n, L, K, n_slots, ft);
     CUDA_TRY(cudaGetLastError());
 
@@ -200,9 +191,6 @@ extern "C" int ft_tbs_batch_device_noalloc(ft_trie *trie, const ft_device_batch 
     sp.topk_id = b->topk_id;
     sp.topk_logp = b->topk_logp;
     sp.factor = reinterpret_cast<const double *>(base + a.factor);
-    sp.row_id = reinterpret_cast<uint32_t *>(base + a.rows_id);
-    sp.row_lp = reinterpret_cast<float *>(base + a.rows_lp);
-    sp.row_orig = reinterpret_cast<uint32_t *>(base + a.rows_orig);
     sp.slots = reinterpret_cast<ftb::SlotView *>(base + a.slots);
     sp.cand_cap = (uint64_t)B * K;
     sp.pool_cap = (uint64_t)B + 2 * (uint64_t)B * K;

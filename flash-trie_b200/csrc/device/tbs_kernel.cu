@@ -12,8 +12,9 @@
 // (throughput).
 //
 // Per step t of a request:
-//   1. every CTA stages row t (ids ascending, log-probs, original columns;
-//      sorted once by row_prep_kernel) in its shared memory;
+//   1. every CTA stages row t (ids ascending, log-probs, original columns)
+//      in its shared memory, straight from the caller's top-k arrays; a row
+//      that is not in id order is bitonic-sorted by (id, column) there;
 //   2. expand:
 //      - in-link beams, one thread each: the next tail cell is the only
 //        allowed token; look it up in the sorted row (tbs-kernels.cu:324-371);
@@ -957,6 +958,53 @@ __device__ void write_result(const SearchParams &p, const SlotView &slot, const 
   if (threadIdx.x == 0) p.out_count[req] = n;
 }
 
+// Stages a row of the caller's top-k arrays in shared memory, ordered by
+// (id, original column): rows already in non-decreasing id order are copied
+// (equal ids keep their column order), others are bitonic-sorted through
+// `scratch` (P2(K) u64 keys, the task table's space).
+__device__ void stage_row(const SearchParams &p, const RowView &row, uint64_t rbase, uint64_t *scratch) {
+  const uint32_t K = row.K;
+  const uint32_t *gid = p.topk_id + rbase;
+  const float *glp = p.topk_logp + rbase;
+  bool ok = true;
+  for (uint32_t j = threadIdx.x; j < K; j += blockDim.x) {
+    const uint32_t id = __ldg(gid + j);
+    row.id[j] = id;
+    row.lp[j] = __ldg(glp + j);
+    row.orig[j] = j;
+    if (j + 1 < K && id > __ldg(gid + j + 1)) ok = false;
+  }
+  if (__syncthreads_and(ok)) return;
+  uint32_t P2 = 1;
+  while (P2 < K) P2 <<= 1;
+  for (uint32_t j = threadIdx.x; j < P2; j += blockDim.x)
+    scratch[j] = j < K ? (((uint64_t)row.id[j] << 32) | j) : ~0ull;
+  __syncthreads();
+  for (uint32_t kk = 2; kk <= P2; kk <<= 1) {
+    for (uint32_t j = kk >> 1; j > 0; j >>= 1) {
+      for (uint32_t i = threadIdx.x; i < P2; i += blockDim.x) {
+        const uint32_t ixj = i ^ j;
+        if (ixj > i) {
+          const uint64_t a = scratch[i], b = scratch[ixj];
+          const bool up = (i & kk) == 0;
+          if ((a > b) == up) {
+            scratch[i] = b;
+            scratch[ixj] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (uint32_t j = threadIdx.x; j < K; j += blockDim.x) {
+    const uint32_t o = (uint32_t)(scratch[j] & 0xFFFFFFFFu);
+    row.id[j] = (uint32_t)(scratch[j] >> 32);
+    row.lp[j] = __ldg(glp + o);
+    row.orig[j] = o;
+  }
+  __syncthreads();
+}
+
 __device__ void reset_counters(StepCounters *s) {
   s->n_next = 0;
   s->key_min = 0xFFFFFFFFu;
@@ -1083,12 +1131,7 @@ __device__ void search_request(const SearchParams &p, uint32_t req, const SlotVi
       trimmed = false;
     }
     if (S->stop || S->n_in + S->n_br == 0 || (p.early_exit && S->pushes >= final_beam)) break;
-    const uint64_t rbase = meta.rows_off + (uint64_t)t * K;
-    for (uint32_t j = threadIdx.x; j < K; j += blockDim.x) {
-      row.id[j] = p.row_id[rbase + j];
-      row.lp[j] = p.row_lp[rbase + j];
-      row.orig[j] = p.row_orig[rbase + j];
-    }
+    stage_row(p, row, meta.rows_off + (uint64_t)t * K, reinterpret_cast<uint64_t *>(bt.info));
     __syncthreads();
     unsigned long long t1 = 0;
     if (leader) t1 = global_ns();
@@ -1203,78 +1246,27 @@ __global__ void __launch_bounds__(kSearchThreads, 1) tbs_search_kernel(const Sea
   }
 }
 
-// Sorts each row by (id, original column) so the search can binary-search it;
-// rows that are already strictly ascending are copied as they are.
-__global__ void row_prep_kernel(const ReqMeta *meta, const uint32_t *ids, const float *lps, uint32_t *out_id,
-                                float *out_lp, uint32_t *out_orig, uint32_t n_req) {
-  extern __shared__ __align__(16) uint8_t dyn[];
-  uint64_t *keys = reinterpret_cast<uint64_t *>(dyn);
-  const uint32_t r = blockIdx.y, t = blockIdx.x;
-  if (r >= n_req) return;
-  const ReqMeta m = meta[r];
-  if (t >= m.L) return;
-  const uint32_t K = m.K;
-  const uint64_t base = m.rows_off + (uint64_t)t * K;
-  bool ok = true;
-  for (uint32_t j = threadIdx.x; j + 1 < K; j += blockDim.x)
-    if (ids[base + j] >= ids[base + j + 1]) ok = false;
-  if (__syncthreads_and(ok)) {
-    for (uint32_t j = threadIdx.x; j < K; j += blockDim.x) {
-      out_id[base + j] = ids[base + j];
-      out_lp[base + j] = lps[base + j];
-      out_orig[base + j] = j;
-    }
-    return;
-  }
-  uint32_t P2 = 1;
-  while (P2 < K) P2 <<= 1;
-  for (uint32_t j = threadIdx.x; j < P2; j += blockDim.x)
-    keys[j] = j < K ? (((uint64_t)ids[base + j] << 32) | j) : ~0ull;
-  __syncthreads();
-  for (uint32_t kk = 2; kk <= P2; kk <<= 1) {
-    for (uint32_t j = kk >> 1; j > 0; j >>= 1) {
-      for (uint32_t i = threadIdx.x; i < P2; i += blockDim.x) {
-        const uint32_t ixj = i ^ j;
-        if (ixj > i) {
-          const uint64_t a = keys[i], b = keys[ixj];
-          const bool up = (i & kk) == 0;
-          if ((a > b) == up) {
-            keys[i] = b;
-            keys[ixj] = a;
-          }
-        }
-      }
-      __syncthreads();
-    }
-  }
-  for (uint32_t j = threadIdx.x; j < K; j += blockDim.x) {
-    const uint32_t o = (uint32_t)(keys[j] & 0xFFFFFFFFu);
-    out_id[base + j] = (uint32_t)(keys[j] >> 32);
-    out_lp[base + j] = lps[base + o];
-    out_orig[base + j] = o;
-  }
-}
-
 }  // namespace
 
 size_t search_smem_bytes(uint32_t max_topk, uint32_t max_final_beam) {
   uint32_t P2 = 1;
   while (P2 < max_final_beam) P2 <<= 1;
+  uint32_t PK = 1;
+  while (PK < max_topk) PK <<= 1;
+  // Row, then the task table (which also holds the sort keys of an unsorted row).
   const size_t row = (((size_t)max_topk * 12 + 15) & ~size_t(15)) +
-                     (size_t)kParentChunk * (sizeof(uint4) + sizeof(double) + sizeof(uint32_t));
+                     std::max<size_t>((size_t)kParentChunk * (sizeof(uint4) + sizeof(double) + sizeof(uint32_t)),
+                                      (size_t)PK * 8);
   const size_t sort = (size_t)P2 * 16;
   return std::max<size_t>(std::max(row, sort), 16);
 }
 
-int ensure_search_smem(size_t search_smem, size_t prep_smem) {
+int ensure_search_smem(size_t search_smem) {
   cudaFuncAttributes a;
   CUDA_TRY(cudaFuncGetAttributes(&a, tbs_search_kernel));
   if ((size_t)a.maxDynamicSharedSizeBytes < search_smem)
     CUDA_TRY(cudaFuncSetAttribute(tbs_search_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)search_smem));
   CUDA_TRY(cudaFuncSetAttribute(tbs_search_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
-  CUDA_TRY(cudaFuncGetAttributes(&a, row_prep_kernel));
-  if ((size_t)a.maxDynamicSharedSizeBytes < prep_smem)
-    CUDA_TRY(cudaFuncSetAttribute(row_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem));
   int per_sm = 0;
   CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tbs_search_kernel, kSearchThreads, search_smem));
   int dev = 0, sms = 0;
@@ -1324,12 +1316,6 @@ int pick_cluster_size(uint32_t n, size_t smem_bytes, int *max_teams) {
 void launch_search(const SearchParams &p, uint32_t max_K, uint32_t max_L, size_t smem_bytes, int grid,
                    cudaStream_t stream, int cluster_size) {
   if (p.n_req == 0) return;
-  uint32_t P2 = 1;
-  while (P2 < max_K) P2 <<= 1;
-  dim3 pg(max_L, p.n_req);
-  row_prep_kernel<<<pg, 256, (size_t)P2 * 8, stream>>>(p.meta, p.topk_id, p.topk_logp, p.row_id, p.row_lp,
-                                                       p.row_orig, p.n_req);
-  CUDA_TRY(cudaGetLastError());
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid * cluster_size, 1, 1);
   cfg.blockDim = dim3(kSearchThreads, 1, 1);

@@ -102,10 +102,6 @@ struct SearchParams {
   const uint32_t *topk_id;
   const float *topk_logp;
   const double *factor;     // [max L + 1]: (6 / (5 + depth)) ^ length_norm
-  // sorted rows (written by the row-prep kernel)
-  uint32_t *row_id;
-  float *row_lp;
-  uint32_t *row_orig;
   // workspace
   SlotView *slots;
   uint64_t cand_cap;
@@ -139,7 +135,7 @@ constexpr uint32_t kStatusSelection = 32u;  // a selection did not select exactl
 // Shared-memory bytes the search kernel needs for a given max K / max final beam.
 size_t search_smem_bytes(uint32_t max_topk, uint32_t max_final_beam);
 
-// Enqueues the row-prep kernel and the search kernel on `stream`: `grid`
+// Enqueues the search kernel on `stream`: `grid`
 // teams of `cluster_size` CTAs (thread-block clusters), one team per
 // in-flight request.  `max_K`, `max_L` bound every request of the batch.
 void launch_search(const SearchParams &p, uint32_t max_K, uint32_t max_L, size_t smem_bytes, int grid,
@@ -152,9 +148,8 @@ int max_search_clusters(int cluster_size, size_t smem_bytes);
 // n teams fitting on the device (FT_CLUSTER_SIZE overrides).
 int pick_cluster_size(uint32_t n, size_t smem_bytes, int *max_teams);
 
-// Raises (never lowers) the dynamic shared-memory limits of the search and
-// row-prep kernels on the current device; returns max resident search CTAs
-// for `search_smem`.
-int ensure_search_smem(size_t search_smem, size_t prep_smem);
+// Raises (never lowers) the dynamic shared-memory limit of the search kernel
+// on the current device; returns max resident search CTAs for `search_smem`.
+int ensure_search_smem(size_t search_smem);
 
 }  // namespace ftb

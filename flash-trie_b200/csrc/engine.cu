@@ -39,7 +39,7 @@ Engine::Engine(std::shared_ptr<DeviceTrie> trie, const EngineLimits &lim) : trie
     throw InvalidArgument("init_tbs_gpu: max_num_out_beams must be in [1, " + std::to_string(kMaxBeams) + "]");
   CUDA_TRY(cudaGetDevice(&device_));
   smem_ = search_smem_bytes((uint32_t)lim.max_topk, (uint32_t)lim.max_out_beams);
-  max_ctas_ = ensure_search_smem(smem_, 64 * 1024);
+  max_ctas_ = ensure_search_smem(smem_);
   n_slots_ = (uint32_t)std::min<uint64_t>(lim.max_batch, (uint64_t)max_ctas_);
 
   const uint64_t B = lim.max_out_beams, K = lim.max_topk, L = lim.max_outpos, NB = lim.max_batch;
@@ -56,9 +56,6 @@ Engine::Engine(std::shared_ptr<DeviceTrie> trie, const EngineLimits &lim) : trie
     }
     d_slots_ = (SlotView *)dalloc(sizeof(SlotView) * n_slots_);
     CUDA_TRY(cudaMemcpy(d_slots_, slots.data(), sizeof(SlotView) * n_slots_, cudaMemcpyHostToDevice));
-    d_row_id_ = (uint32_t *)dalloc(4 * NB * L * K);
-    d_row_lp_ = (float *)dalloc(4 * NB * L * K);
-    d_row_orig_ = (uint32_t *)dalloc(4 * NB * L * K);
     d_status_ = (uint32_t *)dalloc(16);
     CUDA_TRY(cudaMemset(d_status_, 0, 16));
     d_status_dev_ = (uint32_t *)dalloc(16);
@@ -121,9 +118,6 @@ void Engine::validate_request(const ft_request &r) const {
 void Engine::fill_params(SearchParams &sp, const ft_search_params &prm, uint32_t n_req) const {
   std::memset(&sp, 0, sizeof(sp));
   sp.trie = make_trie_view(*trie_);
-  sp.row_id = d_row_id_;
-  sp.row_lp = d_row_lp_;
-  sp.row_orig = d_row_orig_;
   sp.slots = d_slots_;
   sp.cand_cap = lim_.max_out_beams * lim_.max_topk;
   sp.pool_cap = lim_.max_out_beams + 2 * lim_.max_out_beams * lim_.max_topk;

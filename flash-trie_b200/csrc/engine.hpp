@@ -69,9 +69,6 @@ class Engine {
   std::vector<DevBuf> allocs_;
   // device workspace
   SlotView *d_slots_ = nullptr;
-  uint32_t *d_row_id_ = nullptr;
-  float *d_row_lp_ = nullptr;
-  uint32_t *d_row_orig_ = nullptr;
   uint32_t *d_status_ = nullptr;      // host-buffer path: cleared per call
   uint32_t *d_status_dev_ = nullptr;  // device path: accumulates until read
   uint32_t *d_debug_ = nullptr;       // first failed kernel self-check
