@@ -450,54 +450,153 @@ __device__ __forceinline__ uint32_t pick_mode(uint32_t d, uint32_t K, uint32_t f
   return kModeBin;
 }
 
-// A child `child` (node record r) of a branching parent matched sorted-row
-// column m: the candidate and pool entry it yields (tbs-kernels.cu:295-317).
-__device__ __forceinline__ void emit_child(const Ctx &c, double pscore, uint32_t parent_idx, uint32_t child,
-                                           const uint4 &r, uint32_t m) {
-  const double lp = (double)c.row.lp[m];
-  if (lp <= c.p->token_threshold || pscore + lp <= c.p->sent_threshold) return;
-  const double score = pscore + lp;
-  const uint32_t token = c.row.id[m];
-  const uint32_t f = rec_flags(r.w);
-  if (!(f & kNodeFlagLink)) {
-    push_next(c, score, child, r.y, parent_idx, token, r.z, r.w);
-    if (f & kNodeFlagTerminal) push_pool(c, score, child, parent_idx, token);
-  } else if (f & kNodeFlagLinkEnds1) {
-    // The link's string ended with its first token (tbs-kernels.cu:310-313).
-    if (f & kNodeFlagTerminal) push_pool(c, score, child, parent_idx, token);
+// What a matched child yields (tbs-kernels.cu:295-317): a candidate unless it
+// is a link child whose string ends with its first token; a pool entry if it
+// ends a key there (a terminal plain child, or a terminal link child whose
+// string ends with its first token).
+__device__ __forceinline__ void classify(uint32_t f, bool &next, bool &pool) {
+  const bool link = f & kNodeFlagLink, ends1 = link && (f & kNodeFlagLinkEnds1);
+  next = !ends1;
+  pool = (f & kNodeFlagTerminal) && (!link || ends1);
+}
+
+// Reserves `n` consecutive slots per lane from a team counter with one atomic
+// for the whole warp; returns this lane's first slot.  Called by all 32 lanes.
+__device__ __forceinline__ uint32_t warp_reserve(uint32_t *counter, uint32_t n) {
+  const uint32_t lane = threadIdx.x & 31;
+  uint32_t inc = n;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+    if (lane >= (uint32_t)o) inc += y;
+  }
+  const uint32_t total = __shfl_sync(0xFFFFFFFFu, inc, 31);
+  uint32_t base = 0;
+  if (lane == 0 && total) base = atomicAdd(counter, total);
+  return __shfl_sync(0xFFFFFFFFu, base, 0) + inc - n;
+}
+
+__device__ __forceinline__ void write_next(const Ctx &c, uint32_t idx, double score, uint32_t node, uint32_t aux,
+                                           uint32_t parent, uint32_t token, uint32_t c0, uint32_t dw) {
+  const uint32_t k32 = (uint32_t)(orderable(score * c.f_next) >> 32);
+  c.kmin = min(c.kmin, k32);
+  c.kmax = max(c.kmax, k32);
+  if (idx < c.p->cand_cap) {
+    Cand v;
+    v.score = score;
+    v.node = node;
+    v.aux = aux;
+    v.parent = parent;
+    v.token = token;
+    v.c0 = c0;
+    v.dw = dw;
+    c.slot.next[idx] = v;
   } else {
-    push_next(c, score, child, r.y + 1, parent_idx, token, r.z, r.w);
+    atomicOr(c.p->status, kStatusCandOverflow);
   }
 }
 
-// Lookup tasks: a lane's four items issue each round of loads (records,
-// probes) before using any.
+__device__ __forceinline__ void write_pool(const Ctx &c, uint32_t idx, double score, uint32_t node, uint32_t parent,
+                                           uint32_t token) {
+  const uint32_t k32 = (uint32_t)(orderable(score * c.f_next) >> 32);
+  c.pkmin = min(c.pkmin, k32);
+  c.pkmax = max(c.pkmax, k32);
+  if (idx < c.p->pool_cap) {
+    Cand v;
+    v.score = score;
+    v.node = node;
+    v.aux = c.step + 1;  // depth
+    v.parent = parent;
+    v.token = token;
+    v.c0 = 0;
+    v.dw = 0;
+    c.slot.pool[idx] = v;
+  } else {
+    atomicOr(c.p->status, kStatusPoolOverflow);
+  }
+}
+
+// A task's matches: (item k, row column m) pairs, each with the child's record.
+// `visit(k, m)` is called for every pair whose log-prob passes the thresholds.
+// The warp counts its candidates and pool entries first, reserves them with
+// one atomic each, then writes them.
+template <class Pairs>
+__device__ __forceinline__ void emit_task(const Ctx &c, double pscore, uint32_t parent_idx, const uint32_t child[4],
+                                          const uint4 rec[4], Pairs &&pairs) {
+  const double tt = c.p->token_threshold, st = c.p->sent_threshold;
+  uint32_t nn = 0, np = 0;
+  pairs([&](uint32_t k, uint32_t m) {
+    const double lp = (double)c.row.lp[m];
+    if (lp <= tt || pscore + lp <= st) return;
+    bool nx, pl;
+    classify(rec[k].w >> 24, nx, pl);
+    nn += nx;
+    np += pl;
+  });
+  uint32_t bn = warp_reserve(&c.cnt->n_next, nn);
+  uint32_t bp = warp_reserve(&c.T->pool_end, np);
+  if (nn + np == 0) return;
+  pairs([&](uint32_t k, uint32_t m) {
+    const double lp = (double)c.row.lp[m];
+    if (lp <= tt || pscore + lp <= st) return;
+    const double score = pscore + lp;
+    const uint32_t token = c.row.id[m];
+    const uint4 &r = rec[k];
+    bool nx, pl;
+    classify(r.w >> 24, nx, pl);
+    const bool link = (r.w >> 24) & kNodeFlagLink;
+    if (nx) write_next(c, bn++, score, child[k], link ? r.y + 1 : r.y, parent_idx, token, r.z, r.w);
+    if (pl) write_pool(c, bp++, score, child[k], parent_idx, token);
+  });
+}
+
+// Lower bounds of four ids in the sorted row, advanced in lockstep (branch
+// free, the same number of steps for all).
+__device__ __forceinline__ void row_lower_bound4(const RowView &r, const uint32_t x[4], uint32_t pos[4]) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) pos[k] = 0;
+  if (r.K == 0) return;
+  for (uint32_t n = r.K; n > 1;) {
+    const uint32_t half = n >> 1;
+    uint32_t v[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) v[k] = r.id[pos[k] + half - 1];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) pos[k] = v[k] < x[k] ? pos[k] + half : pos[k];
+    n -= half;
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    if (r.id[pos[k]] < x[k]) ++pos[k];
+}
+
+// Lookup tasks (called by all 32 lanes of a warp): a lane's four items issue
+// each round of loads before using any.
 __device__ __forceinline__ void task_scan(const Ctx &c, uint32_t c0, uint32_t d, uint32_t first_item, double score,
                                           uint32_t parent_idx) {
   const TrieView &t = c.p->trie;
   const uint32_t lane = threadIdx.x & 31;
   uint4 rec[kItemsPerLane];
-  uint32_t mlo[kItemsPerLane];
+  uint32_t child[kItemsPerLane], x[kItemsPerLane], mlo[kItemsPerLane];
 #pragma unroll
   for (uint32_t k = 0; k < kItemsPerLane; ++k) {
     const uint32_t i = first_item + 32u * k + lane;
+    child[k] = c0 + i;
     rec[k] = i < d ? __ldg(t.node + c0 + i) : make_uint4(0, 0, 0, 0);
   }
 #pragma unroll
-  for (uint32_t k = 0; k < kItemsPerLane; ++k) {
-    const uint32_t i = first_item + 32u * k + lane;
-    mlo[k] = c.row.K;
-    if (i < d) {
-      const uint32_t m = row_lower_bound(c.row, rec[k].x);
-      if (m < c.row.K && c.row.id[m] == rec[k].x) mlo[k] = m;
-    }
-  }
+  for (uint32_t k = 0; k < kItemsPerLane; ++k) x[k] = rec[k].x;
+  row_lower_bound4(c.row, x, mlo);
 #pragma unroll
   for (uint32_t k = 0; k < kItemsPerLane; ++k) {
-    const uint32_t child = c0 + first_item + 32u * k + lane;
-    for (uint32_t m = mlo[k]; m < c.row.K && c.row.id[m] == rec[k].x; ++m)
-      emit_child(c, score, parent_idx, child, rec[k], m);
+    const uint32_t i = first_item + 32u * k + lane;
+    if (i >= d || mlo[k] >= c.row.K || c.row.id[mlo[k]] != x[k]) mlo[k] = c.row.K;
   }
+  emit_task(c, score, parent_idx, child, rec, [&](auto &&fn) {
+#pragma unroll
+    for (uint32_t k = 0; k < kItemsPerLane; ++k)
+      for (uint32_t m = mlo[k]; m < c.row.K && c.row.id[m] == x[k]; ++m) fn(k, m);
+  });
 }
 
 __device__ __forceinline__ void task_hash(const Ctx &c, uint32_t base, uint32_t lg, uint32_t first_item, double score,
@@ -529,6 +628,7 @@ __device__ __forceinline__ void task_hash(const Ctx &c, uint32_t base, uint32_t 
 #pragma unroll
   for (uint32_t k = 0; k < kItemsPerLane; ++k) {
     child[k] = 0;
+    rec[k] = make_uint4(0, 0, 0, 0);
     if (!on[k]) continue;
     uint2 sl = slot[k];
     uint32_t hk = h[k];
@@ -539,9 +639,11 @@ __device__ __forceinline__ void task_hash(const Ctx &c, uint32_t base, uint32_t 
     child[k] = sl.y;
     if (child[k] != 0) rec[k] = __ldg(t.node + child[k]);
   }
+  emit_task(c, score, parent_idx, child, rec, [&](auto &&fn) {
 #pragma unroll
-  for (uint32_t k = 0; k < kItemsPerLane; ++k)
-    if (child[k] != 0) emit_child(c, score, parent_idx, child[k], rec[k], first_item + 32u * k + lane);
+    for (uint32_t k = 0; k < kItemsPerLane; ++k)
+      if (child[k] != 0) fn(k, first_item + 32u * k + lane);
+  });
 }
 
 __device__ __forceinline__ void task_bin(const Ctx &c, uint32_t c0, uint32_t d, uint32_t first_item, double score,
@@ -551,7 +653,7 @@ __device__ __forceinline__ void task_bin(const Ctx &c, uint32_t c0, uint32_t d, 
   const uint32_t lane = threadIdx.x & 31;
   // Labels are the first word of each 16-byte record.
   const uint32_t *labs = reinterpret_cast<const uint32_t *>(t.node + c0);
-  uint32_t x[kItemsPerLane], pos[kItemsPerLane];
+  uint32_t x[kItemsPerLane], pos[kItemsPerLane], child[kItemsPerLane];
   uint4 rec[kItemsPerLane];
   bool on[kItemsPerLane];
 #pragma unroll
@@ -579,22 +681,20 @@ __device__ __forceinline__ void task_bin(const Ctx &c, uint32_t c0, uint32_t d, 
   }
 #pragma unroll
   for (uint32_t k = 0; k < kItemsPerLane; ++k) {
+    child[k] = 0;
+    rec[k] = make_uint4(0, 0, 0, 0);
     if (on[k] && d > 0) {
-      uint32_t p = pos[k];
-      if (__ldg(labs + 4u * p) < x[k]) ++p;
-      pos[k] = p;
-      on[k] = p < d;
-    } else {
-      on[k] = false;
+      uint32_t q = pos[k];
+      if (__ldg(labs + 4u * q) < x[k]) ++q;
+      if (q < d && __ldg(labs + 4u * q) == x[k]) child[k] = c0 + q;
     }
-    if (on[k]) {
-      rec[k] = __ldg(t.node + c0 + pos[k]);
-      on[k] = rec[k].x == x[k];
-    }
+    if (child[k] != 0) rec[k] = __ldg(t.node + child[k]);
   }
+  emit_task(c, score, parent_idx, child, rec, [&](auto &&fn) {
 #pragma unroll
-  for (uint32_t k = 0; k < kItemsPerLane; ++k)
-    if (on[k]) emit_child(c, score, parent_idx, c0 + pos[k], rec[k], first_item + 32u * k + lane);
+    for (uint32_t k = 0; k < kItemsPerLane; ++k)
+      if (child[k] != 0) fn(k, first_item + 32u * k + lane);
+  });
 }
 
 // Branching beams, per chunk of parents: every CTA builds the same task table
