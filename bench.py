@@ -191,6 +191,31 @@ class DeviceBatch(ctypes.Structure):
                                                        "out_len", "out_tok")]
 
 
+# ncu captures of the search kernel summarised under profiles/ (one launch
+# each): (config, batch, beam, keys) -> summary file holding the measured
+# dram__bytes_read.sum + dram__bytes_write.sum of that launch.
+PROFILED = {
+    (2, 1, 100, 10_000_000): "tbs_search_kernel_config2_batch1.md",
+    (3, 32, 1000, 50_000_000): "tbs_search_kernel_config3_beam1000_batch32.md",
+}
+
+
+def measured_traffic(args, cfg):
+    """DRAM bytes per launch from the profile summary of this workload, or
+    (None, None) when it was not captured."""
+    name = PROFILED.get((args.config, cfg["batch"], cfg["beam"], cfg["keys"]))
+    if not name:
+        return None, None
+    try:
+        with open(os.path.join(REPO, "profiles", name)) as f:
+            for line in f:
+                if line.startswith("dram_bytes_per_launch:"):
+                    return int(line.split(":")[1]), "profiles/" + name
+    except OSError:
+        pass
+    return None, None
+
+
 def algorithmic_bytes(path, beams, ids, lp, cfg):
     """Per-request algorithmic bytes from the oracle's byte model (test
     infrastructure used as the checker/counter only)."""
@@ -452,6 +477,7 @@ def run_b200(args, cfg):
         bytes_per_launch = float(np.mean([per_req_bytes[i:i + nb].sum() for i in used]))
         peak, peak_kind = measured_peaks()
         achieved = bytes_per_launch / (float(step_ms.mean()) / 1e3) / 1e9
+        traffic, traffic_src = measured_traffic(args, cfg)
         cpu_qps, cpu_ms, cpu_n, cpu_wall = (None, [], 0, 0.0)
         ref_built = os.path.isdir(os.path.join(REPO, "oracle", "_ref")) and any(
             f.startswith("flashtrie_ref") for f in os.listdir(os.path.join(REPO, "oracle", "_ref")))
@@ -473,8 +499,8 @@ def run_b200(args, cfg):
                     "path": "flashtrie.bs_tbs_gpu (numpy host buffers)",
                     "binding_ms": {"mean": float(np.mean(binding_ms)), "p99": float(np.percentile(binding_ms, 99))}},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None, "peak_source": peak_kind,
-                         "bytes_alg_per_launch": bytes_per_launch},
+                         "frac": achieved / peak, "traffic": traffic, "traffic_source": traffic_src,
+                         "peak_source": peak_kind, "bytes_alg_per_launch": bytes_per_launch},
             "cpu_baseline": ({"value": cpu_qps, "unit": UNIT, "cores": 1, "kind": "reference",
                               "sample": "%d requests of config %d, %.1f s, reference tbs(use_gpu=False), 1 core"
                                         % (cpu_n, args.config, cpu_wall)} if cpu_qps else None),
