@@ -200,6 +200,8 @@ struct alignas(16) LocalState {
   uint32_t sel_rem;
   int sel_ge;
   uint32_t pass;  // radix passes run by the team in this request
+  uint32_t out_total;               // tokens of the request's result (compact output)
+  unsigned long long out_base;      // their first slot
   uint32_t stop;
 };
 
@@ -996,8 +998,12 @@ __device__ void trim_pool(const Ctx &c, uint32_t n, uint32_t k) {
 }
 
 // Sorts the final pool (descending) and writes the ascending result (rank 0).
+// With p.tok_total set, each request's tokens are written contiguously (beam
+// by beam in output order) at an offset it reserves from that counter, stored
+// in p.out_tok_base; otherwise beam o of request r starts at slot (r*cap + o)
+// of p.out_tok with stride p.out_stride.
 __device__ void write_result(const SearchParams &p, const SlotView &slot, const Cand *pool, uint32_t n, uint32_t req,
-                             uint8_t *dyn) {
+                             uint8_t *dyn, LocalState *S) {
   uint32_t P2 = 1;
   while (P2 < n) P2 <<= 1;
   ulonglong2 *items = reinterpret_cast<ulonglong2 *>(dyn);
@@ -1030,6 +1036,38 @@ __device__ void write_result(const SearchParams &p, const SlotView &slot, const 
     }
   }
   const uint32_t cap = p.out_cap, stride = p.out_stride;
+  const bool compact = p.tok_total != nullptr;
+  uint64_t tok_base = 0;
+  if (compact) {
+    // Output beam o = n-1-s starts after the tokens of every beam s' > s.
+    // items[s].x (the sort key, no longer needed) takes the length, then
+    // the offset.
+    for (uint32_t s = threadIdx.x; s < n; s += blockDim.x) {
+      const uint32_t d = ld_cand(pool + (uint32_t)(items[s].y & 0xFFFFu)).aux;
+      items[s].x = (d == 0 || d > stride) ? 0 : d;
+    }
+    __syncthreads();
+    const uint32_t per = (n + blockDim.x - 1) / blockDim.x;
+    const uint32_t s0 = min(n, threadIdx.x * per), s1 = min(n, s0 + per);
+    uint32_t mine = 0;
+    for (uint32_t s = s0; s < s1; ++s) mine += (uint32_t)items[s].x;
+    uint32_t run = block_exclusive_sum(mine, S);
+    if (threadIdx.x == blockDim.x - 1) S->out_total = run + mine;  // the request's token total
+    __syncthreads();
+    const uint32_t total = S->out_total;
+    for (uint32_t s = s0; s < s1; ++s) {
+      const uint32_t len = (uint32_t)items[s].x;
+      items[s].x = total - run - len;
+      run += len;
+    }
+    if (threadIdx.x == 0) {
+      const uint64_t b = total ? atomicAdd(reinterpret_cast<unsigned long long *>(p.tok_total), (unsigned long long)total) : 0ull;
+      p.out_tok_base[req] = b;
+      S->out_base = b;
+    }
+    __syncthreads();
+    tok_base = S->out_base;
+  }
   for (uint32_t s = threadIdx.x; s < n; s += blockDim.x) {
     const uint32_t idx = (uint32_t)(items[s].y & 0xFFFFu);
     const Cand v = ld_cand(pool + idx);
@@ -1042,7 +1080,7 @@ __device__ void write_result(const SearchParams &p, const SlotView &slot, const 
     }
     p.out_lpn[slot_o] = depth ? v.score * p.factor[depth] : 0.0;
     p.out_len[slot_o] = depth;
-    uint32_t *tok = p.out_tok + slot_o * stride;
+    uint32_t *tok = compact ? p.out_tok + tok_base + items[s].x : p.out_tok + slot_o * stride;
     if (depth) tok[depth - 1] = v.token;
     uint32_t j = v.parent;
     for (uint32_t st = depth ? depth - 1 : 0; st >= 1; --st) {
@@ -1317,7 +1355,7 @@ __device__ void search_request(const SearchParams &p, uint32_t req, const SlotVi
     }
   }
   if (rank == 0) {
-    write_result(p, slot, out_pool, n_out, req, dyn);
+    write_result(p, slot, out_pool, n_out, req, dyn, S);
     if (threadIdx.x == 0 && p.out_phase_ms) {
       const unsigned long long t5 = global_ns();
       double *ph = p.out_phase_ms + (uint64_t)req * 5;

@@ -121,6 +121,8 @@ struct SearchParams {
   uint32_t *out_len;
   uint32_t *out_tok;
   double *out_phase_ms;  // [n_req][5] or nullptr
+  uint64_t *tok_total;   // compact token output: running token count, or nullptr (strided output)
+  uint64_t *out_tok_base;  // compact token output: [n_req] first token of each request
   uint32_t *status;      // device status word (bit flags, see kStatus*)
   uint32_t *debug;       // [8]: first failed self-check (code, step, n, k, got, team, ge, rem)
 };

@@ -1,5 +1,7 @@
 #include "engine.hpp"
 
+#include <omp.h>
+
 #include <cmath>
 #include <cstring>
 #include <string>
@@ -66,7 +68,7 @@ Engine::Engine(std::shared_ptr<DeviceTrie> trie, const EngineLimits &lim) : trie
     in_bytes_ = align16(sizeof(ReqMeta) * NB) + align16(8 * (L + 1)) + align16(4 * NB * L) + 2 * align16(4 * NB * L * K);
     d_in_ = (uint8_t *)dalloc(in_bytes_);
     CUDA_TRY(cudaMallocHost(&h_in_, in_bytes_));
-    out_bytes_ = 16 + align16(4 * NB) + align16(8 * 5 * NB) + align16(8 * NB * B) + align16(4 * NB * B) +
+    out_bytes_ = 16 + align16(4 * NB) + align16(8 * 5 * NB) + align16(8 * NB * B) + align16(4 * NB * B) + align16(8 * NB) +
                  align16(4 * NB * B * L);
     d_out_ = (uint8_t *)dalloc(out_bytes_);
     CUDA_TRY(cudaMallocHost(&h_out_, out_bytes_));
@@ -170,23 +172,32 @@ void Engine::search_host(const ft_request *reqs, uint32_t n, const ft_search_par
   for (uint32_t i = 0; i < n; ++i) {
     const ft_request &r = reqs[i];
     meta[i] = ReqMeta{r.num_outpos, r.topk, bo, ro};
-    std::memcpy(hb + bo, r.beams, 4ull * r.num_outpos);
+    bo += r.num_outpos;
+    ro += (uint64_t)r.num_outpos * r.topk;
+  }
+  // Large batches are copied into the pinned buffer by several threads.
+  const int pack_threads = sum_LK * 8 > (4u << 20) ? std::min(16, omp_get_max_threads()) : 1;
+#pragma omp parallel for schedule(dynamic, 1) num_threads(pack_threads)
+  for (int64_t i = 0; i < (int64_t)n; ++i) {
+    const ft_request &r = reqs[i];
+    std::memcpy(hb + meta[i].beams_off, r.beams, 4ull * r.num_outpos);
     const uint64_t lk = (uint64_t)r.num_outpos * r.topk;
     if (lk) {
-      std::memcpy(hid + ro, r.topk_id, 4 * lk);
-      std::memcpy(hlp + ro, r.topk_logp, 4 * lk);
+      std::memcpy(hid + meta[i].rows_off, r.topk_id, 4 * lk);
+      std::memcpy(hlp + meta[i].rows_off, r.topk_logp, 4 * lk);
     }
-    bo += r.num_outpos;
-    ro += lk;
   }
   CUDA_TRY(cudaMemcpyAsync(d_in_, h_in_, in_used, cudaMemcpyHostToDevice, stream_));
 
-  // Output region [status | count | phase | lpn | len | tok] for this batch.
+  // Output region [status, token total | count | phase | lpn | len | token base | tok] for this
+  // batch; tokens are written compactly (each request's at the base it reserves), so only the
+  // tokens actually produced need to come back.
   const uint32_t stride = max_L;
   const size_t q_count = 16, q_phase = q_count + align16(4 * n), q_lpn = q_phase + align16(8 * 5 * n),
-               q_len = q_lpn + align16(8ull * n * cap), q_tok = q_len + align16(4ull * n * cap),
-               out_used = q_tok + align16(4ull * n * cap * stride);
+               q_len = q_lpn + align16(8ull * n * cap), q_base = q_len + align16(4ull * n * cap),
+               q_tok = q_base + align16(8ull * n), tok_bytes_max = 4ull * n * cap * stride;
   CUDA_TRY(cudaMemsetAsync(d_status_, 0, 4, stream_));
+  CUDA_TRY(cudaMemsetAsync(d_out_ + 8, 0, 8, stream_));
 
   SearchParams sp;
   fill_params(sp, prm, n);
@@ -202,13 +213,25 @@ void Engine::search_host(const ft_request *reqs, uint32_t n, const ft_search_par
   sp.out_lpn = reinterpret_cast<double *>(d_out_ + q_lpn);
   sp.out_len = reinterpret_cast<uint32_t *>(d_out_ + q_len);
   sp.out_tok = reinterpret_cast<uint32_t *>(d_out_ + q_tok);
+  sp.tok_total = reinterpret_cast<uint64_t *>(d_out_ + 8);
+  sp.out_tok_base = reinterpret_cast<uint64_t *>(d_out_ + q_base);
   int max_teams = 1;
   const int cs = pick_cluster_size(n, smem_, &max_teams);
   const int grid = (int)std::min<uint32_t>(std::min<uint32_t>(n, n_slots_), (uint32_t)max_teams);
   launch_search(sp, max_K, max_L, smem_, grid, stream_, cs);
   CUDA_TRY(cudaMemcpyAsync(d_out_, d_status_, 4, cudaMemcpyDeviceToDevice, stream_));
-  CUDA_TRY(cudaMemcpyAsync(h_out_, d_out_, out_used, cudaMemcpyDeviceToHost, stream_));
+  // Small batches: everything in one copy.  Large ones: the headers first,
+  // then only the tokens produced.
+  const bool two_phase = tok_bytes_max > kOneCopyTokenBytes;
+  CUDA_TRY(cudaMemcpyAsync(h_out_, d_out_, two_phase ? q_tok : q_tok + tok_bytes_max, cudaMemcpyDeviceToHost,
+                           stream_));
   CUDA_TRY(cudaStreamSynchronize(stream_));
+  const uint64_t tok_total = *reinterpret_cast<const uint64_t *>(h_out_ + 8);
+  if (tok_total * 4 > tok_bytes_max) throw std::runtime_error("tbs: the search kernel reported an invalid token total");
+  if (two_phase && tok_total) {
+    CUDA_TRY(cudaMemcpyAsync(h_out_ + q_tok, d_out_ + q_tok, 4 * tok_total, cudaMemcpyDeviceToHost, stream_));
+    CUDA_TRY(cudaStreamSynchronize(stream_));
+  }
 
   const uint32_t status = *reinterpret_cast<const uint32_t *>(h_out_);
   if (status != 0) {
@@ -223,18 +246,23 @@ void Engine::search_host(const ft_request *reqs, uint32_t n, const ft_search_par
   const double *hphase = reinterpret_cast<const double *>(h_out_ + q_phase);
   const double *hlpn = reinterpret_cast<const double *>(h_out_ + q_lpn);
   const uint32_t *hlen = reinterpret_cast<const uint32_t *>(h_out_ + q_len);
+  const uint64_t *hbase = reinterpret_cast<const uint64_t *>(h_out_ + q_base);
   const uint32_t *htok = reinterpret_cast<const uint32_t *>(h_out_ + q_tok);
   for (uint32_t i = 0; i < n; ++i) {
     const uint32_t nb = hcount[i];
     ft_result &r = out[i];
     r.num_beams = nb;
     for (int k = 0; k < 5; ++k) r.phase_ms[k] = hphase[5 * i + k];
+    uint64_t off = nb ? hbase[i] : 0;
     for (uint32_t b = 0; b < nb; ++b) {
       const uint64_t s = (uint64_t)i * cap + b;
       r.logp_norm[b] = hlpn[s];
       const uint32_t len = hlen[s];
+      if (len > r.stride || off + len > tok_total)
+        throw std::runtime_error("tbs: the search kernel returned an inconsistent result layout");
       r.lengths[b] = len;
-      std::memcpy(r.tokens + (uint64_t)b * r.stride, htok + s * stride, 4ull * len);
+      std::memcpy(r.tokens + (uint64_t)b * r.stride, htok + off, 4ull * len);
+      off += len;
     }
   }
 }

@@ -32,6 +32,9 @@ struct EngineLimits {
 constexpr uint64_t kMaxTopk = 8192;
 constexpr uint64_t kMaxBeams = 8192;
 constexpr uint64_t kMaxOutpos = 65535;
+// Result tokens of a host-buffer batch come back in one copy with the headers
+// up to this size, else in a second copy of just the tokens produced.
+constexpr size_t kOneCopyTokenBytes = 256 * 1024;
 
 class InvalidArgument : public std::runtime_error {
  public:

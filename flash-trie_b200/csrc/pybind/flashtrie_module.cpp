@@ -28,6 +28,7 @@
 #include <fstream>
 #include <iostream>
 #include <limits>
+#include <memory>
 #include <numeric>
 #include <sstream>
 #include <stdexcept>
@@ -163,11 +164,16 @@ void PyTrie::build(py::object rows) {
   check(ft_trie_build(h_, tokens.data(), offsets.data(), offsets.size() - 1));
 }
 
-// One request converted to contiguous buffers.
+// One request as contiguous buffers: numpy rows of the right dtype and
+// layout are borrowed (the array objects are kept alive here), lists are
+// converted into owned vectors.
 struct Req {
   std::vector<uint32_t> beams;
-  std::vector<uint32_t> ids;
-  std::vector<float> lp;
+  std::vector<uint32_t> ids_own;
+  std::vector<float> lp_own;
+  py::object ids_keep, lp_keep;
+  const uint32_t *ids = nullptr;
+  const float *lp = nullptr;
   uint32_t L = 0, K = 0;
 };
 
@@ -181,25 +187,29 @@ void convert_request(py::handle beams, py::handle topk_id, py::handle topk_logp,
       throw py::value_error("topk_id and topk_logp must be 2-D arrays of the same shape");
     if ((uint32_t)ai.shape(0) != r.L) throw py::value_error("topk_id must have one row per entry of beams");
     r.K = (uint32_t)ai.shape(1);
-    r.ids.assign(ai.data(), ai.data() + ai.size());
-    r.lp.assign(al.data(), al.data() + al.size());
+    r.ids = ai.data();
+    r.lp = al.data();
+    r.ids_keep = std::move(ai);
+    r.lp_keep = std::move(al);
     return;
   }
   size_t rows_i = 0, rows_l = 0;
   bool first = true;
   for (py::handle row : topk_id) {
-    const size_t k = append_labels(row, r.ids);
+    const size_t k = append_labels(row, r.ids_own);
     if (first) r.K = (uint32_t)k;
     else if (k != r.K) throw py::value_error("all topk_id rows must have the same length");
     first = false;
     ++rows_i;
   }
   for (py::handle row : topk_logp) {
-    const size_t k = append_floats(row, r.lp);
+    const size_t k = append_floats(row, r.lp_own);
     if (k != r.K) throw py::value_error("topk_logp rows must match the topk_id rows");
     ++rows_l;
   }
   if (rows_i != r.L || rows_l != r.L) throw py::value_error("topk_id and topk_logp must have one row per entry of beams");
+  r.ids = r.ids_own.data();
+  r.lp = r.lp_own.data();
 }
 
 double msec_truncated(std::chrono::high_resolution_clock::time_point a, std::chrono::high_resolution_clock::time_point b) {
@@ -211,7 +221,7 @@ double msec_truncated(std::chrono::high_resolution_clock::time_point a, std::chr
 struct Out {
   std::vector<double> lpn;
   std::vector<uint32_t> len;
-  std::vector<uint32_t> tok;
+  std::unique_ptr<uint32_t[]> tok;  // cap * stride slots, only the first len[b] of beam b are written
   ft_result res;
 };
 
@@ -220,13 +230,13 @@ void prepare_out(const Req &r, Out &o) {
   const uint32_t stride = std::max<uint32_t>(r.L, 1);
   o.lpn.assign(cap, 0.0);
   o.len.assign(cap, 0);
-  o.tok.assign((size_t)cap * stride, 0);
+  o.tok.reset(new uint32_t[(size_t)cap * stride]);
   std::memset(&o.res, 0, sizeof(o.res));
   o.res.capacity = cap;
   o.res.stride = stride;
   o.res.logp_norm = o.lpn.data();
   o.res.lengths = o.len.data();
-  o.res.tokens = o.tok.data();
+  o.res.tokens = o.tok.get();
 }
 
 py::list sentences(const Out &o) {
@@ -234,7 +244,7 @@ py::list sentences(const Out &o) {
   for (uint32_t b = 0; b < o.res.num_beams; ++b) {
     const uint32_t n = o.len[b];
     py::list s(n);
-    const uint32_t *t = o.tok.data() + (size_t)b * o.res.stride;
+    const uint32_t *t = o.tok.get() + (size_t)b * o.res.stride;
     for (uint32_t k = 0; k < n; ++k) PyList_SET_ITEM(s.ptr(), k, PyLong_FromUnsignedLong(t[k]));
     PyList_SET_ITEM(l.ptr(), b, s.release().ptr());
   }
@@ -280,7 +290,7 @@ py::tuple tbs(PyTrie &trie, py::object beams, py::object topk_id, py::object top
   if (reqs[0].L == 0) throw py::value_error("tbs: beams must not be empty");
   if (reqs[0].beams[reqs[0].L - 1] != 0) {
     ensure_workspace(trie, reqs);
-    ft_request fr{reqs[0].L, reqs[0].K, reqs[0].beams.data(), reqs[0].ids.data(), reqs[0].lp.data()};
+    ft_request fr{reqs[0].L, reqs[0].K, reqs[0].beams.data(), reqs[0].ids, reqs[0].lp};
     const ft_search_params prm = make_params(tt, st, ln, early_exit);
     py::gil_scoped_release nogil;
     check(ft_tbs_batch(trie.h(), &fr, 1, &prm, &o.res));
@@ -319,7 +329,7 @@ py::tuple bs_tbs_gpu(PyTrie &trie, size_t batch_size, py::object batch_beams, py
     prepare_out(reqs[i], outs[i]);
     if (reqs[i].beams[reqs[i].L - 1] == 0) continue;
     live.push_back(i);
-    fr.push_back(ft_request{reqs[i].L, reqs[i].K, reqs[i].beams.data(), reqs[i].ids.data(), reqs[i].lp.data()});
+    fr.push_back(ft_request{reqs[i].L, reqs[i].K, reqs[i].beams.data(), reqs[i].ids, reqs[i].lp});
   }
   if (!live.empty()) {
     ensure_workspace(trie, reqs);
