@@ -209,10 +209,9 @@ extern "C" int ft_tbs_batch_device_noalloc(ft_trie *trie, const ft_device_batch 
     sp.out_phase_ms = nullptr;
     sp.status = reinterpret_cast<uint32_t *>(base + a.status);
     sp.debug = nullptr;
-    int max_teams = 1;
-    const int cs = ftb::pick_cluster_size(n, smem, &max_teams);
-    const int grid = (int)std::min<uint32_t>(std::min<uint32_t>(n_slots, (uint32_t)max_ctas), (uint32_t)max_teams);
-    ftb::launch_search(sp, K, L, smem, grid, stream, cs);
+    const ftb::SearchLaunch plan = ftb::plan_search(n, smem);
+    const int grid = (int)std::min<uint32_t>(std::min<uint32_t>(n_slots, (uint32_t)max_ctas), (uint32_t)plan.max_teams);
+    ftb::launch_search(sp, smem, grid, stream, plan);
     CUDA_TRY(cudaStreamSynchronize(stream));
     uint32_t status = 0;
     CUDA_TRY(cudaMemcpy(&status, base + a.status, 4, cudaMemcpyDeviceToHost));

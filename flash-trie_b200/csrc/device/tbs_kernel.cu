@@ -1368,7 +1368,13 @@ __device__ void search_request(const SearchParams &p, uint32_t req, const SlotVi
   }
 }
 
-__global__ void __launch_bounds__(kSearchThreads, 1) tbs_search_kernel(const SearchParams p) {
+// Two instances: one CTA per SM with up to 128 registers per thread (all
+// launches with teams of 2-16 CTAs, and batches the SMs can hold one request
+// each), and two CTAs per SM at 64 registers per thread (batches larger than
+// the SM count, where twice the requests in flight hide more latency than the
+// spills cost).
+template <int kMinBlocks>
+__global__ void __launch_bounds__(kSearchThreads, kMinBlocks) tbs_search_kernel(const SearchParams p) {
   extern __shared__ __align__(16) uint8_t dyn[];
   __shared__ TeamState team_state;
   __shared__ LocalState local_state;
@@ -1399,18 +1405,30 @@ size_t search_smem_bytes(uint32_t max_topk, uint32_t max_final_beam) {
   return std::max<size_t>(std::max(row, sort), 16);
 }
 
-int ensure_search_smem(size_t search_smem) {
+template <int kMinBlocks>
+static int raise_smem(size_t search_smem) {
   cudaFuncAttributes a;
-  CUDA_TRY(cudaFuncGetAttributes(&a, tbs_search_kernel));
+  CUDA_TRY(cudaFuncGetAttributes(&a, tbs_search_kernel<kMinBlocks>));
   if ((size_t)a.maxDynamicSharedSizeBytes < search_smem)
-    CUDA_TRY(cudaFuncSetAttribute(tbs_search_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)search_smem));
-  CUDA_TRY(cudaFuncSetAttribute(tbs_search_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    CUDA_TRY(cudaFuncSetAttribute(tbs_search_kernel<kMinBlocks>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)search_smem));
+  CUDA_TRY(cudaFuncSetAttribute(tbs_search_kernel<kMinBlocks>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
   int per_sm = 0;
-  CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tbs_search_kernel, kSearchThreads, search_smem));
+  CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tbs_search_kernel<kMinBlocks>, kSearchThreads,
+                                                         search_smem));
+  return per_sm;
+}
+
+static int sm_count() {
   int dev = 0, sms = 0;
   CUDA_TRY(cudaGetDevice(&dev));
   CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  return std::max(per_sm, 1) * sms;
+  return sms;
+}
+
+int ensure_search_smem(size_t search_smem) {
+  const int one = raise_smem<1>(search_smem), two = raise_smem<2>(search_smem);
+  return std::max(std::max(one, two), 1) * sm_count();
 }
 
 int max_search_clusters(int cluster_size, size_t smem_bytes) {
@@ -1426,14 +1444,13 @@ int max_search_clusters(int cluster_size, size_t smem_bytes) {
   cfg.attrs = &attr;
   cfg.numAttrs = 1;
   int n = 0;
-  CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, (void *)tbs_search_kernel, &cfg));
+  CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, (void *)tbs_search_kernel<1>, &cfg));
   return n;
 }
 
-int pick_cluster_size(uint32_t n, size_t smem_bytes, int *max_teams) {
-  int dev = 0, sms = 0;
-  CUDA_TRY(cudaGetDevice(&dev));
-  CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+SearchLaunch plan_search(uint32_t n, size_t smem_bytes) {
+  const int sms = sm_count();
+  SearchLaunch l;
   int cs = 1;
   if (const char *e = getenv("FT_CLUSTER_SIZE")) {
     cs = atoi(e);
@@ -1445,28 +1462,44 @@ int pick_cluster_size(uint32_t n, size_t smem_bytes, int *max_teams) {
   for (;; cs /= 2) {
     const int teams = max_search_clusters(cs, smem_bytes);
     if (teams >= 1 || cs == 1) {
-      *max_teams = std::max(teams, 1);
-      return cs;
+      l.cluster_size = cs;
+      l.max_teams = std::max(teams, 1);
+      break;
     }
   }
+  l.dense = 0;
+  bool dense_ok = l.cluster_size == 1 && n > (uint32_t)sms;
+  if (const char *e = getenv("FT_DENSE")) dense_ok = l.cluster_size == 1 && atoi(e) != 0;
+  if (dense_ok) {
+    int per_sm = 0;
+    CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tbs_search_kernel<2>, kSearchThreads, smem_bytes));
+    if (per_sm >= 2) {
+      l.dense = 1;
+      l.max_teams = per_sm * sms;
+    }
+  }
+  return l;
 }
 
-void launch_search(const SearchParams &p, uint32_t max_K, uint32_t max_L, size_t smem_bytes, int grid,
-                   cudaStream_t stream, int cluster_size) {
+void launch_search(const SearchParams &p, size_t smem_bytes, int grid, cudaStream_t stream, const SearchLaunch &l) {
   if (p.n_req == 0) return;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid * cluster_size, 1, 1);
+  cfg.gridDim = dim3(grid * l.cluster_size, 1, 1);
   cfg.blockDim = dim3(kSearchThreads, 1, 1);
   cfg.dynamicSmemBytes = smem_bytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr;
   attr.id = cudaLaunchAttributeClusterDimension;
-  attr.val.clusterDim.x = cluster_size;
+  attr.val.clusterDim.x = l.cluster_size;
   attr.val.clusterDim.y = 1;
   attr.val.clusterDim.z = 1;
   cfg.attrs = &attr;
   cfg.numAttrs = 1;
-  CUDA_TRY(cudaLaunchKernelEx(&cfg, tbs_search_kernel, p));
+  if (l.dense) {
+    CUDA_TRY(cudaLaunchKernelEx(&cfg, tbs_search_kernel<2>, p));
+  } else {
+    CUDA_TRY(cudaLaunchKernelEx(&cfg, tbs_search_kernel<1>, p));
+  }
 }
 
 }  // namespace ftb

@@ -137,21 +137,30 @@ constexpr uint32_t kStatusSelection = 32u;  // a selection did not select exactl
 // Shared-memory bytes the search kernel needs for a given max K / max final beam.
 size_t search_smem_bytes(uint32_t max_topk, uint32_t max_final_beam);
 
-// Enqueues the search kernel on `stream`: `grid`
-// teams of `cluster_size` CTAs (thread-block clusters), one team per
-// in-flight request.  `max_K`, `max_L` bound every request of the batch.
-void launch_search(const SearchParams &p, uint32_t max_K, uint32_t max_L, size_t smem_bytes, int grid,
-                   cudaStream_t stream, int cluster_size);
+// How a batch is launched: teams of `cluster_size` CTAs (thread-block
+// clusters), at most `max_teams` resident at once; `dense` selects the
+// two-CTAs-per-SM kernel instance (one-CTA teams, batches larger than the SM
+// count).  FT_CLUSTER_SIZE and FT_DENSE override the choice.
+struct SearchLaunch {
+  int cluster_size;
+  int max_teams;
+  int dense;
+};
+
+// Team size for a batch of n requests: the largest power of two <= 16 with
+// n teams fitting on the device.
+SearchLaunch plan_search(uint32_t n, size_t smem_bytes);
+
+// Enqueues the search kernel on `stream`: `grid` teams, one per in-flight
+// request (requests beyond `grid` are taken by teams that finish).
+void launch_search(const SearchParams &p, size_t smem_bytes, int grid, cudaStream_t stream, const SearchLaunch &l);
 
 // Teams of `cluster_size` CTAs that can be resident at once.
 int max_search_clusters(int cluster_size, size_t smem_bytes);
 
-// Team size for a batch of n requests: the largest power of two <= 16 with
-// n teams fitting on the device (FT_CLUSTER_SIZE overrides).
-int pick_cluster_size(uint32_t n, size_t smem_bytes, int *max_teams);
-
-// Raises (never lowers) the dynamic shared-memory limit of the search kernel
-// on the current device; returns max resident search CTAs for `search_smem`.
+// Raises (never lowers) the dynamic shared-memory limit of both search kernel
+// instances on the current device; returns max resident search CTAs for
+// `search_smem` (of the denser instance).
 int ensure_search_smem(size_t search_smem);
 
 }  // namespace ftb

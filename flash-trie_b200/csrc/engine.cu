@@ -215,10 +215,9 @@ void Engine::search_host(const ft_request *reqs, uint32_t n, const ft_search_par
   sp.out_tok = reinterpret_cast<uint32_t *>(d_out_ + q_tok);
   sp.tok_total = reinterpret_cast<uint64_t *>(d_out_ + 8);
   sp.out_tok_base = reinterpret_cast<uint64_t *>(d_out_ + q_base);
-  int max_teams = 1;
-  const int cs = pick_cluster_size(n, smem_, &max_teams);
-  const int grid = (int)std::min<uint32_t>(std::min<uint32_t>(n, n_slots_), (uint32_t)max_teams);
-  launch_search(sp, max_K, max_L, smem_, grid, stream_, cs);
+  const SearchLaunch plan = plan_search(n, smem_);
+  const int grid = (int)std::min<uint32_t>(std::min<uint32_t>(n, n_slots_), (uint32_t)plan.max_teams);
+  launch_search(sp, smem_, grid, stream_, plan);
   CUDA_TRY(cudaMemcpyAsync(d_out_, d_status_, 4, cudaMemcpyDeviceToDevice, stream_));
   // Small batches: everything in one copy.  Large ones: the headers first,
   // then only the tokens produced.
@@ -301,10 +300,9 @@ void Engine::search_device(const ft_device_batch &b, const ft_search_params &prm
   sp.out_tok = b.out_tok;
   sp.out_phase_ms = nullptr;
   sp.status = d_status_dev_;
-  int max_teams = 1;
-  const int cs = pick_cluster_size(b.n, smem_, &max_teams);
-  const int grid = (int)std::min<uint32_t>(std::min<uint32_t>(b.n, n_slots_), (uint32_t)max_teams);
-  launch_search(sp, K, L, smem_, grid, stream, cs);
+  const SearchLaunch plan = plan_search(b.n, smem_);
+  const int grid = (int)std::min<uint32_t>(std::min<uint32_t>(b.n, n_slots_), (uint32_t)plan.max_teams);
+  launch_search(sp, smem_, grid, stream, plan);
 }
 
 uint32_t Engine::read_status() {

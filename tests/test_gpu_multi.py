@@ -108,3 +108,23 @@ def test_sharded_world2_nccl(built, tmp_path):
         assert pr.exitcode == 0
     res = sorted(q.get(timeout=10) for _ in range(2))
     assert all(ok for _, ok in res), res
+
+
+@pytest.mark.parametrize("dense", ["0", "1"])
+def test_batch_beyond_sm_count_matches_oracle(built, tmp_path, monkeypatch, dense):
+    """300 requests: more than one per SM, so one-CTA teams take requests in
+    turn; with FT_DENSE=1 the two-CTAs-per-SM kernel instance runs them."""
+    import flashtrie
+    from oracle.oracle import OracleTrie
+    monkeypatch.setenv("FT_DENSE", dense)
+    p, tok, off, cfg = _small_trie(tmp_path, n_keys=30000, seed=11)
+    n = 300
+    beams, ids, lp = W.gen_requests(1, tok, off, n, cfg=cfg)
+    t = flashtrie.Trie()
+    t.load(p)
+    t.init_tbs_gpu(n, max_num_topk=cfg["K"], max_num_outpos=cfg["L"], max_num_out_beams=cfg["beam"])
+    sents, lpns, _, _ = flashtrie.bs_tbs_gpu(t, n, beams, ids, lp, -10.0, -40.0, 5.0, False)
+    o = OracleTrie(p)
+    for i in range(n):
+        o_s, o_l = o.tbs(beams[i], ids[i], lp[i], -10.0, -40.0, 5.0, False)
+        assert same_result(sents[i], lpns[i], o_s, o_l), i
