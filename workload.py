@@ -216,4 +216,8 @@ def gen_keys_torch(n, vocab, len_lo, len_hi, zipf_s, seed, device="cuda"):
     offsets = torch.zeros(n + 1, dtype=torch.int64, device=dev)
     torch.cumsum(lens, 0, out=offsets[1:])
     tokens = mat[cols[None, :] < lens[:, None]]
-    return tokens.cpu().numpy().view(np.uint32), offsets.cpu().numpy().astype(np.uint64)
+    out = tokens.cpu().numpy().view(np.uint32), offsets.cpu().numpy().astype(np.uint64)
+    del tokens, mat, lens, offsets, keep, alll, cdf, w, cols, g
+    if dev.type == "cuda":
+        torch.cuda.empty_cache()  # the scratch of 10^8+ keys is tens of GB; hand it back
+    return out
