@@ -188,7 +188,7 @@ class DeviceBatch(ctypes.Structure):
     _fields_ = [("n", ctypes.c_uint32), ("num_outpos", ctypes.c_uint32), ("topk", ctypes.c_uint32),
                 ("out_capacity", ctypes.c_uint32)] + [(f, ctypes.c_void_p) for f in
                                                       ("beams", "topk_id", "topk_logp", "out_count", "out_lpn",
-                                                       "out_len", "out_tok")]
+                                                       "out_len", "out_tok", "out_key")]
 
 
 # ncu captures of the search kernel summarised under profiles/ (one launch

@@ -172,12 +172,13 @@ void DeviceTrie::release() {
     cudaGetDevice(&prev);
     cudaSetDevice(device);
     cudaFree(node);
+    cudaFree(term_rank);
     cudaFree(tail);
     cudaFree(tail_end);
     cudaFree(hash);
     if (prev >= 0) cudaSetDevice(prev);
   }
-  node = tail = nullptr;
+  node = term_rank = tail = nullptr;
   tail_end = nullptr;
   hash = nullptr;
   hash_slots = 0;
@@ -209,6 +210,24 @@ void DeviceTrie::upload(const LoudsLevel &lv, int num_threads) {
       std::vector<uint32_t> rec;
       pack_node_records(img, rec, num_threads);
       node = upload_array(rec.data(), rec.size(), bytes);
+    }
+    {
+      // Key-id directory over the terminal flags.
+      const uint64_t blocks = (num_nodes + 63) / 64;
+      if (lv.terminal.units.size() < blocks) fail(ErrorKind::kFormat, "MARISA_FORMAT_ERROR: terminal flags too short");
+      std::vector<uint32_t> tr(4 * blocks, 0);
+      uint64_t cum = 0;
+      for (uint64_t b = 0; b < blocks; ++b) {
+        uint64_t bits = lv.terminal.units[b];
+        const uint64_t valid = num_nodes - b * 64;
+        if (valid < 64) bits &= (1ull << valid) - 1;
+        tr[4 * b] = (uint32_t)cum;
+        tr[4 * b + 2] = (uint32_t)bits;
+        tr[4 * b + 3] = (uint32_t)(bits >> 32);
+        cum += (uint64_t)__builtin_popcountll(bits);
+      }
+      if (cum >= 0xFFFFFFFFull) fail(ErrorKind::kSize, "MARISA_SIZE_ERROR: too many keys for 32-bit key ids");
+      term_rank = upload_array(tr.data(), tr.size(), bytes);
     }
     tail = upload_array(lv.tail.data(), lv.tail.size(), bytes);
     if (binary_tail) tail_end = upload_array(lv.tail_end_flags.units.data(), lv.tail_end_flags.units.size(), bytes);

@@ -21,6 +21,10 @@
 //             log2 of the table size);
 //     fan-out min(number of children, 0xFFFFFF); 0xFFFFFF means "at least
 //             that many": the range then ends at node[n + 1].c0 (or N).
+//   term_rank per 64 nodes {u32 terminal nodes before the block, u32 0, u64 the
+//             block's terminal bits}: a key's id is the rank of its terminal
+//             node among terminal nodes (LoudsTrie::lookup, louds-trie.cc:56-72),
+//             one 16-byte load;
 //   tail      u32 cells as stored in the file (0xFFFFFFFF terminates a string
 //             in a text tail); tail_end: end bits of a binary tail.
 //   hash      per-node open-addressing tables for plain (non-link) nodes with
@@ -69,6 +73,7 @@ struct DeviceTrie {
   uint64_t tail_size = 0;
   bool binary_tail = false;
   uint32_t *node = nullptr;  // [4 * num_nodes]: {label, aux, c0, flags << 24 | fan-out}
+  uint32_t *term_rank = nullptr;  // [4 * ceil(num_nodes / 64)], see above
   uint32_t *tail = nullptr;
   uint64_t *tail_end = nullptr;
   uint32_t *hash = nullptr;

@@ -206,6 +206,7 @@ extern "C" int ft_tbs_batch_device_noalloc(ft_trie *trie, const ft_device_batch 
     sp.out_lpn = b->out_lpn;
     sp.out_len = b->out_len;
     sp.out_tok = b->out_tok;
+    sp.out_key = b->out_key;
     sp.out_phase_ms = nullptr;
     sp.status = reinterpret_cast<uint32_t *>(base + a.status);
     sp.debug = nullptr;

@@ -145,6 +145,14 @@ __device__ __forceinline__ Beam ld_beam(const Beam *p) {
 
 __device__ __forceinline__ uint32_t rec_flags(uint32_t dw) { return dw >> 24; }
 
+// Key id of a terminal node: terminal nodes before it (louds-trie.cc:56-72).
+__device__ __forceinline__ uint32_t key_id(const TrieView &t, uint32_t node) {
+  const uint4 r = __ldg(t.term_rank + (node >> 6));
+  const uint64_t bits = ((uint64_t)r.w << 32) | r.z;
+  const uint32_t o = node & 63u;
+  return r.x + (uint32_t)__popcll(o ? bits & ((1ull << o) - 1) : 0ull);
+}
+
 __device__ __forceinline__ Hist ld_hist(const Hist *p) {
   const uint2 a = __ldcg(reinterpret_cast<const uint2 *>(p));
   return Hist{a.x, a.y};
@@ -1080,6 +1088,8 @@ __device__ void write_result(const SearchParams &p, const SlotView &slot, const 
     }
     p.out_lpn[slot_o] = depth ? v.score * p.factor[depth] : 0.0;
     p.out_len[slot_o] = depth;
+    if (p.out_key)
+      p.out_key[slot_o] = (uint64_t)v.node < p.trie.num_nodes ? key_id(p.trie, v.node) : 0xFFFFFFFFu;
     uint32_t *tok = compact ? p.out_tok + tok_base + items[s].x : p.out_tok + slot_o * stride;
     if (depth) tok[depth - 1] = v.token;
     uint32_t j = v.parent;

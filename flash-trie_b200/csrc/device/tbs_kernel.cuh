@@ -57,6 +57,7 @@ struct ReqMeta {
 
 struct TrieView {
   const uint4 *node;
+  const uint4 *term_rank;    // key-id directory, see device_trie.hpp
   const uint32_t *tail;
   const uint64_t *tail_end;  // nullptr for a text tail
   const uint2 *hash;         // per-node child tables {label, child}, see device_trie.hpp
@@ -68,6 +69,7 @@ struct TrieView {
 inline TrieView make_trie_view(const DeviceTrie &d) {
   TrieView v;
   v.node = reinterpret_cast<const uint4 *>(d.node);
+  v.term_rank = reinterpret_cast<const uint4 *>(d.term_rank);
   v.tail = d.tail;
   v.tail_end = d.binary_tail ? d.tail_end : nullptr;
   v.hash = reinterpret_cast<const uint2 *>(d.hash);
@@ -120,6 +122,7 @@ struct SearchParams {
   double *out_lpn;
   uint32_t *out_len;
   uint32_t *out_tok;
+  uint32_t *out_key;     // [n_req][out_cap] key ids of the result beams, or nullptr
   double *out_phase_ms;  // [n_req][5] or nullptr
   uint64_t *tok_total;   // compact token output: running token count, or nullptr (strided output)
   uint64_t *out_tok_base;  // compact token output: [n_req] first token of each request

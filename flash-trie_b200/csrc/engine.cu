@@ -68,7 +68,8 @@ Engine::Engine(std::shared_ptr<DeviceTrie> trie, const EngineLimits &lim) : trie
     in_bytes_ = align16(sizeof(ReqMeta) * NB) + align16(8 * (L + 1)) + align16(4 * NB * L) + 2 * align16(4 * NB * L * K);
     d_in_ = (uint8_t *)dalloc(in_bytes_);
     CUDA_TRY(cudaMallocHost(&h_in_, in_bytes_));
-    out_bytes_ = 16 + align16(4 * NB) + align16(8 * 5 * NB) + align16(8 * NB * B) + align16(4 * NB * B) + align16(8 * NB) +
+    out_bytes_ = 16 + align16(4 * NB) + align16(8 * 5 * NB) + align16(8 * NB * B) + 2 * align16(4 * NB * B) +
+                 align16(8 * NB) +
                  align16(4 * NB * B * L);
     d_out_ = (uint8_t *)dalloc(out_bytes_);
     CUDA_TRY(cudaMallocHost(&h_out_, out_bytes_));
@@ -189,13 +190,16 @@ void Engine::search_host(const ft_request *reqs, uint32_t n, const ft_search_par
   }
   CUDA_TRY(cudaMemcpyAsync(d_in_, h_in_, in_used, cudaMemcpyHostToDevice, stream_));
 
-  // Output region [status, token total | count | phase | lpn | len | token base | tok] for this
-  // batch; tokens are written compactly (each request's at the base it reserves), so only the
-  // tokens actually produced need to come back.
+  // Output region [status, token total | count | phase | lpn | len | key | token base | tok] for
+  // this batch; tokens are written compactly (each request's at the base it reserves), so only
+  // the tokens actually produced need to come back.
   const uint32_t stride = max_L;
+  bool want_keys = false;
+  for (uint32_t i = 0; i < n; ++i) want_keys |= out[i].key_ids != nullptr;
   const size_t q_count = 16, q_phase = q_count + align16(4 * n), q_lpn = q_phase + align16(8 * 5 * n),
-               q_len = q_lpn + align16(8ull * n * cap), q_base = q_len + align16(4ull * n * cap),
-               q_tok = q_base + align16(8ull * n), tok_bytes_max = 4ull * n * cap * stride;
+               q_len = q_lpn + align16(8ull * n * cap), q_key = q_len + align16(4ull * n * cap),
+               q_base = q_key + (want_keys ? align16(4ull * n * cap) : 0), q_tok = q_base + align16(8ull * n),
+               tok_bytes_max = 4ull * n * cap * stride;
   CUDA_TRY(cudaMemsetAsync(d_status_, 0, 4, stream_));
   CUDA_TRY(cudaMemsetAsync(d_out_ + 8, 0, 8, stream_));
 
@@ -213,6 +217,7 @@ void Engine::search_host(const ft_request *reqs, uint32_t n, const ft_search_par
   sp.out_lpn = reinterpret_cast<double *>(d_out_ + q_lpn);
   sp.out_len = reinterpret_cast<uint32_t *>(d_out_ + q_len);
   sp.out_tok = reinterpret_cast<uint32_t *>(d_out_ + q_tok);
+  sp.out_key = want_keys ? reinterpret_cast<uint32_t *>(d_out_ + q_key) : nullptr;
   sp.tok_total = reinterpret_cast<uint64_t *>(d_out_ + 8);
   sp.out_tok_base = reinterpret_cast<uint64_t *>(d_out_ + q_base);
   const SearchLaunch plan = plan_search(n, smem_);
@@ -246,6 +251,7 @@ void Engine::search_host(const ft_request *reqs, uint32_t n, const ft_search_par
   const double *hlpn = reinterpret_cast<const double *>(h_out_ + q_lpn);
   const uint32_t *hlen = reinterpret_cast<const uint32_t *>(h_out_ + q_len);
   const uint64_t *hbase = reinterpret_cast<const uint64_t *>(h_out_ + q_base);
+  const uint32_t *hkey = reinterpret_cast<const uint32_t *>(h_out_ + q_key);
   const uint32_t *htok = reinterpret_cast<const uint32_t *>(h_out_ + q_tok);
   for (uint32_t i = 0; i < n; ++i) {
     const uint32_t nb = hcount[i];
@@ -260,6 +266,7 @@ void Engine::search_host(const ft_request *reqs, uint32_t n, const ft_search_par
       if (len > r.stride || off + len > tok_total)
         throw std::runtime_error("tbs: the search kernel returned an inconsistent result layout");
       r.lengths[b] = len;
+      if (r.key_ids) r.key_ids[b] = hkey[s];
       std::memcpy(r.tokens + (uint64_t)b * r.stride, htok + off, 4ull * len);
       off += len;
     }
@@ -298,6 +305,7 @@ void Engine::search_device(const ft_device_batch &b, const ft_search_params &prm
   sp.out_lpn = b.out_lpn;
   sp.out_len = b.out_len;
   sp.out_tok = b.out_tok;
+  sp.out_key = b.out_key;
   sp.out_phase_ms = nullptr;
   sp.status = d_status_dev_;
   const SearchLaunch plan = plan_search(b.n, smem_);

@@ -17,6 +17,9 @@
 // Lists of lists are accepted as in the reference; numpy arrays of matching
 // shape are read without per-element conversion.  Every search runs on the
 // B200 engine (`use_gpu` is accepted for signature compatibility).
+// Extension: keyword-only return_key_ids=True appends the key id of every
+// result beam (LoudsTrie::lookup's id, louds-trie.cc:56-72) to the returned
+// tuple: tbs -> (..., ms, key_ids), bs_tbs_gpu -> (..., phase_times, key_ids).
 #include <pybind11/numpy.h>
 #include <pybind11/pybind11.h>
 #include <pybind11/stl.h>
@@ -221,11 +224,12 @@ double msec_truncated(std::chrono::high_resolution_clock::time_point a, std::chr
 struct Out {
   std::vector<double> lpn;
   std::vector<uint32_t> len;
+  std::vector<uint32_t> key;  // key ids, when asked for
   std::unique_ptr<uint32_t[]> tok;  // cap * stride slots, only the first len[b] of beam b are written
   ft_result res;
 };
 
-void prepare_out(const Req &r, Out &o) {
+void prepare_out(const Req &r, Out &o, bool keys) {
   const uint32_t cap = std::max<uint32_t>(r.L ? r.beams[r.L - 1] : 0, 1);
   const uint32_t stride = std::max<uint32_t>(r.L, 1);
   o.lpn.assign(cap, 0.0);
@@ -237,6 +241,16 @@ void prepare_out(const Req &r, Out &o) {
   o.res.logp_norm = o.lpn.data();
   o.res.lengths = o.len.data();
   o.res.tokens = o.tok.get();
+  if (keys) {
+    o.key.assign(cap, 0);
+    o.res.key_ids = o.key.data();
+  }
+}
+
+py::list key_ids(const Out &o) {
+  py::list l(o.res.num_beams);
+  for (uint32_t b = 0; b < o.res.num_beams; ++b) PyList_SET_ITEM(l.ptr(), b, PyLong_FromUnsignedLong(o.key[b]));
+  return l;
 }
 
 py::list sentences(const Out &o) {
@@ -281,12 +295,12 @@ ft_search_params make_params(float tt, double st, double ln, bool ee) {
 }
 
 py::tuple tbs(PyTrie &trie, py::object beams, py::object topk_id, py::object topk_logp, float tt, double st,
-              double ln, bool early_exit, bool /*use_gpu*/) {
+              double ln, bool early_exit, bool /*use_gpu*/, bool return_key_ids) {
   std::vector<Req> reqs(1);
   convert_request(beams, topk_id, topk_logp, reqs[0]);
   const auto start = std::chrono::high_resolution_clock::now();
   Out o;
-  prepare_out(reqs[0], o);
+  prepare_out(reqs[0], o, return_key_ids);
   if (reqs[0].L == 0) throw py::value_error("tbs: beams must not be empty");
   if (reqs[0].beams[reqs[0].L - 1] != 0) {
     ensure_workspace(trie, reqs);
@@ -296,11 +310,13 @@ py::tuple tbs(PyTrie &trie, py::object beams, py::object topk_id, py::object top
     check(ft_tbs_batch(trie.h(), &fr, 1, &prm, &o.res));
   }
   const auto end = std::chrono::high_resolution_clock::now();
+  if (return_key_ids) return py::make_tuple(sentences(o), scores(o), msec_truncated(start, end), key_ids(o));
   return py::make_tuple(sentences(o), scores(o), msec_truncated(start, end));
 }
 
 py::tuple bs_tbs_gpu(PyTrie &trie, size_t batch_size, py::object batch_beams, py::object batch_topk_id,
-                     py::object batch_topk_logp, float tt, double st, double ln, bool early_exit) {
+                     py::object batch_topk_logp, float tt, double st, double ln, bool early_exit,
+                     bool return_key_ids) {
   const size_t nb = (size_t)py::len(batch_beams), ni = (size_t)py::len(batch_topk_id),
                nl = (size_t)py::len(batch_topk_logp);
   if (nb != batch_size || ni != batch_size || nl != batch_size)
@@ -326,7 +342,7 @@ py::tuple bs_tbs_gpu(PyTrie &trie, size_t batch_size, py::object batch_beams, py
   std::vector<ft_result> res;
   std::vector<size_t> live;  // requests with a non-zero final beam (tbs-kernels.cu:692-697)
   for (size_t i = 0; i < batch_size; ++i) {
-    prepare_out(reqs[i], outs[i]);
+    prepare_out(reqs[i], outs[i], return_key_ids);
     if (reqs[i].beams[reqs[i].L - 1] == 0) continue;
     live.push_back(i);
     fr.push_back(ft_request{reqs[i].L, reqs[i].K, reqs[i].beams.data(), reqs[i].ids, reqs[i].lp});
@@ -342,14 +358,16 @@ py::tuple bs_tbs_gpu(PyTrie &trie, size_t batch_size, py::object batch_beams, py
     for (size_t k = 0; k < live.size(); ++k) outs[live[k]].res = res[k];
   }
   const auto end = std::chrono::high_resolution_clock::now();
-  py::list sents(batch_size), lpns(batch_size), phases(batch_size);
+  py::list sents(batch_size), lpns(batch_size), phases(batch_size), keys(return_key_ids ? batch_size : 0);
   for (size_t i = 0; i < batch_size; ++i) {
+    if (return_key_ids) PyList_SET_ITEM(keys.ptr(), i, key_ids(outs[i]).release().ptr());
     PyList_SET_ITEM(sents.ptr(), i, sentences(outs[i]).release().ptr());
     PyList_SET_ITEM(lpns.ptr(), i, scores(outs[i]).release().ptr());
     py::list ph(5);
     for (int k = 0; k < 5; ++k) PyList_SET_ITEM(ph.ptr(), k, PyFloat_FromDouble(outs[i].res.phase_ms[k]));
     PyList_SET_ITEM(phases.ptr(), i, ph.release().ptr());
   }
+  if (return_key_ids) return py::make_tuple(sents, lpns, msec_truncated(start, end), phases, keys);
   return py::make_tuple(sents, lpns, msec_truncated(start, end), phases);
 }
 
@@ -460,9 +478,10 @@ PYBIND11_MODULE(flashtrie, m) {
 
   m.def("tbs", &tbs, py::arg("trie"), py::arg("beams"), py::arg("topk_id"), py::arg("topk_logp"),
         py::arg("token_logp_threshold"), py::arg("sents_logp_threshold"), py::arg("length_norm"),
-        py::arg("early_exit"), py::arg("use_gpu") = false);
+        py::arg("early_exit"), py::arg("use_gpu") = false, py::kw_only(), py::arg("return_key_ids") = false);
   m.def("bs_tbs_gpu", &bs_tbs_gpu, py::arg("trie"), py::arg("batch_size"), py::arg("batch_beams"),
         py::arg("batch_topk_id"), py::arg("batch_topk_logp"), py::arg("token_logp_threshold"),
-        py::arg("sents_logp_threshold"), py::arg("length_norm"), py::arg("early_exit"));
+        py::arg("sents_logp_threshold"), py::arg("length_norm"), py::arg("early_exit"), py::kw_only(),
+        py::arg("return_key_ids") = false);
   m.def("load_topk_keys_and_scores", &load_topk_keys_and_scores, py::arg("dataset_dir"));
 }

@@ -17,7 +17,8 @@ Inputs (contiguous, on one CUDA device): beams int32 [n, L]; topk_id int32
 [n, L, K] (token ids, read as unsigned); topk_logp float32 [n, L, K].  Rows
 need not be sorted by id.  Outputs: count int32 [n]; logp_norm float64
 [n, cap] ascending; lengths int32 [n, cap]; tokens int32 [n, cap, L], beam j
-of request i in tokens[i, j, :lengths[i, j]].
+of request i in tokens[i, j, :lengths[i, j]]; with key_ids=True also key ids
+int32 [n, cap] (LoudsTrie::lookup's id of each result, read as unsigned).
 """
 import ctypes
 import os
@@ -38,7 +39,7 @@ class _Batch(ctypes.Structure):
     _fields_ = [("n", ctypes.c_uint32), ("num_outpos", ctypes.c_uint32), ("topk", ctypes.c_uint32),
                 ("out_capacity", ctypes.c_uint32)] + [(f, ctypes.c_void_p) for f in
                                                       ("beams", "topk_id", "topk_logp", "out_count", "out_lpn",
-                                                       "out_len", "out_tok")]
+                                                       "out_len", "out_tok", "out_key")]
 
 
 def _lib():
@@ -79,9 +80,10 @@ def device_status(trie):
 
 
 def bs_tbs_device(trie, beams, topk_id, topk_logp, token_logp_threshold, sents_logp_threshold, length_norm,
-                  early_exit, capacity=None, stream=None, check=True):
+                  early_exit, capacity=None, stream=None, check=True, key_ids=False):
     """Searches n requests whose inputs are CUDA tensors; returns
-    (count, logp_norm, lengths, tokens) as CUDA tensors on the same device.
+    (count, logp_norm, lengths, tokens[, keys]) as CUDA tensors on the same
+    device (keys with key_ids=True).
 
     capacity: result slots per request (>= every final beam width); default
     beams[:, -1].max(), which reads one value back from the device.
@@ -104,10 +106,12 @@ def bs_tbs_device(trie, beams, topk_id, topk_logp, token_logp_threshold, sents_l
     lpn = torch.empty((n, capacity), dtype=torch.float64, device=dev)
     lens = torch.zeros((n, capacity), dtype=torch.int32, device=dev)
     toks = torch.empty((n, capacity, max(L, 1)), dtype=torch.int32, device=dev)
+    keys = torch.full((n, capacity), -1, dtype=torch.int32, device=dev) if key_ids else None
+    out = (count, lpn, lens, toks) + ((keys,) if key_ids else ())
     if n == 0:
-        return count, lpn, lens, toks
+        return out
     b = _Batch(n, L, K, capacity, beams.data_ptr(), topk_id.data_ptr(), topk_logp.data_ptr(), count.data_ptr(),
-               lpn.data_ptr(), lens.data_ptr(), toks.data_ptr())
+               lpn.data_ptr(), lens.data_ptr(), toks.data_ptr(), keys.data_ptr() if key_ids else None)
     prm = _Params(float(token_logp_threshold), 0.0, float(sents_logp_threshold), float(length_norm),
                   int(bool(early_exit)), 0)
     if stream is None:
@@ -119,16 +123,19 @@ def bs_tbs_device(trie, beams, topk_id, topk_logp, token_logp_threshold, sents_l
         st = device_status(trie)
         if st:
             raise RuntimeError("device search failed its self-checks or exceeded the workspace (status 0x%x)" % st)
-    return count, lpn, lens, toks
+    return out
 
 
 def to_lists(out):
-    """(count, logp_norm, lengths, tokens) -> (sentences, logp_norms) as host
-    lists in the layout bs_tbs_gpu returns."""
-    count, lpn, lens, toks = (t.cpu() for t in out)
-    sents, lpns = [], []
+    """(count, logp_norm, lengths, tokens[, keys]) -> (sentences, logp_norms
+    [, key_ids]) as host lists in the layout bs_tbs_gpu returns."""
+    host = [t.cpu() for t in out]
+    count, lpn, lens, toks = host[:4]
+    sents, lpns, keys = [], [], []
     for i in range(count.shape[0]):
         c = int(count[i])
         sents.append([(toks[i, j, :int(lens[i, j])].numpy().view("uint32")).tolist() for j in range(c)])
         lpns.append(lpn[i, :c].tolist())
-    return sents, lpns
+        if len(host) > 4:
+            keys.append(host[4][i, :c].numpy().view("uint32").tolist())
+    return (sents, lpns, keys) if len(host) > 4 else (sents, lpns)

@@ -73,6 +73,10 @@ typedef struct {
   uint32_t *tokens;           /* out: [capacity*stride], beam i at i*stride  */
   double phase_ms[5];         /* out: expansion, validation, selection,
                                  overhead, kernel (tbs_input.h:19-25)        */
+  uint32_t *key_ids;          /* out, optional ([capacity], NULL: not written):
+                                 the key id of each beam, as LoudsTrie::lookup
+                                 reports it (louds-trie.cc:56-72; no
+                                 counterpart in the reference's TbsInput)    */
 } ft_result;
 
 /* Search parameters shared by a batch (tools/bindings.cpp:71-78). */
@@ -138,6 +142,7 @@ int ft_tbs_batch(ft_trie *trie, const ft_request *requests, uint32_t n,
  *   out_lpn   f64 [n][cap]       ascending logp_norm
  *   out_len   u32 [n][cap]
  *   out_tok   u32 [n][cap][L]
+ *   out_key   u32 [n][cap]       key ids (optional, NULL: not written)
  * `stream` is a cudaStream_t (0 = default stream).  The call returns after
  * enqueueing; completion is observed with stream synchronisation.
  */
@@ -153,6 +158,7 @@ typedef struct {
   double *out_lpn;
   uint32_t *out_len;
   uint32_t *out_tok;
+  uint32_t *out_key;
 } ft_device_batch;
 
 int ft_tbs_batch_device(ft_trie *trie, const ft_device_batch *batch,

@@ -48,6 +48,8 @@ def lib():
         L.oracle_num_keys.restype = ctypes.c_uint64
         L.oracle_lookup.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32]
         L.oracle_lookup.restype = ctypes.c_int
+        L.oracle_lookup_id.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32]
+        L.oracle_lookup_id.restype = ctypes.c_int64
         L.oracle_tbs.argtypes = [
             ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p,
             ctypes.c_void_p, ctypes.c_float, ctypes.c_double, ctypes.c_double, ctypes.c_int,
@@ -84,6 +86,11 @@ class OracleTrie:
     def lookup(self, key):
         a = np.ascontiguousarray(key, dtype=np.uint32)
         return bool(lib().oracle_lookup(self._h, _ptr(a), len(a)))
+
+    def lookup_id(self, key):
+        """Key id (reference LoudsTrie::lookup), or -1."""
+        a = np.ascontiguousarray(key, dtype=np.uint32)
+        return int(lib().oracle_lookup_id(self._h, _ptr(a), len(a)))
 
     def tbs(self, beams, topk_id, topk_logp, token_logp_threshold, sents_logp_threshold,
             length_norm, early_exit, stats=False):

@@ -43,8 +43,12 @@ CXX_OBJS := $(patsubst %.cc,$(OBJ)/%.o,$(CXX_SRCS))
 BIND_OBJ := $(OBJ)/tools/bindings.o
 DLINK    := $(OBJ)/dlink.o
 MODULE   := $(OUT)/flashtrie_ref$(EXT)
+# The reference's own key-id lookup tool (tools/marisa-lookup.cc): pins the
+# key ids the engine reports against the reference's LoudsTrie::lookup.
+LOOKUP   := $(OUT)/marisa-lookup
+TOOL_OBJS := $(OBJ)/tools/marisa-lookup.o $(OBJ)/tools/cmdopt.o
 
-all: $(MODULE)
+all: $(MODULE) $(LOOKUP)
 
 $(CU_OBJS): $(OBJ)/%.o: $(REF)/%.cc
 	@mkdir -p $(dir $@)
@@ -65,6 +69,13 @@ $(DLINK): $(CU_OBJS)
 
 $(MODULE): $(CU_OBJS) $(CXX_OBJS) $(BIND_OBJ) $(DLINK)
 	$(CXX) -shared -fopenmp -o $@ $^ -L/usr/local/cuda/lib64 -lcudart -Wl,-rpath,/usr/local/cuda/lib64
+
+$(TOOL_OBJS): $(OBJ)/tools/%.o: $(REF)/tools/%.cc
+	@mkdir -p $(dir $@)
+	$(CXX) $(CXXFLAGS) -I$(REF)/tools -c $< -o $@
+
+$(LOOKUP): $(CU_OBJS) $(CXX_OBJS) $(TOOL_OBJS) $(DLINK)
+	$(CXX) -fopenmp -o $@ $^ -L/usr/local/cuda/lib64 -lcudart -Wl,-rpath,/usr/local/cuda/lib64
 
 clean:
 	rm -rf $(OUT)

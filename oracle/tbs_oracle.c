@@ -273,16 +273,16 @@ static uint32_t tail_next(const oracle_trie *t, uint64_t *off, int *end) {
   return tok;
 }
 
-int oracle_lookup(const oracle_trie *t, const uint32_t *key, uint32_t len) {
-  /* Walk the trie following the reference LoudsTrie::find_child
-   * (louds-trie.cc:764-808) with a text/binary tail match. */
+/* Node reached by `key` (reference LoudsTrie::find_child, louds-trie.cc:764-808,
+ * with a text/binary tail match), or -1. */
+static int64_t walk(const oracle_trie *t, const uint32_t *key, uint32_t len) {
   uint64_t node = 0;
   uint32_t pos = 0;
   while (pos < len) {
     uint64_t lp = select0(&t->louds, node) + 1;
     uint64_t child;
     int found = 0;
-    if (!bit_get(&t->louds, lp)) return 0;
+    if (!bit_get(&t->louds, lp)) return -1;
     child = lp - node - 1;
     for (; bit_get(&t->louds, lp); ++lp, ++child) {
       if (bit_get(&t->link, child)) {
@@ -291,7 +291,7 @@ int oracle_lookup(const oracle_trie *t, const uint32_t *key, uint32_t len) {
         for (;;) {
           int end;
           uint32_t tok = tail_next(t, &off, &end);
-          if (pos >= len || tok != key[pos]) return 0;
+          if (pos >= len || tok != key[pos]) return -1;
           pos++;
           if (end) break;
         }
@@ -303,10 +303,23 @@ int oracle_lookup(const oracle_trie *t, const uint32_t *key, uint32_t len) {
         break;
       }
     }
-    if (!found) return 0;
+    if (!found) return -1;
     node = child;
   }
-  return bit_get(&t->terminal, node);
+  return (int64_t)node;
+}
+
+int oracle_lookup(const oracle_trie *t, const uint32_t *key, uint32_t len) {
+  const int64_t node = walk(t, key, len);
+  return node >= 0 && bit_get(&t->terminal, (uint64_t)node);
+}
+
+/* Key id of `key`: the rank of its terminal node among the terminal nodes
+ * (reference LoudsTrie::lookup, louds-trie.cc:56-72), or -1. */
+int64_t oracle_lookup_id(const oracle_trie *t, const uint32_t *key, uint32_t len) {
+  const int64_t node = walk(t, key, len);
+  if (node < 0 || !bit_get(&t->terminal, (uint64_t)node)) return -1;
+  return (int64_t)rank1(&t->terminal, (uint64_t)node);
 }
 
 /* ------------------------------------------------------------ search */

@@ -55,6 +55,9 @@ uint64_t oracle_num_keys(const oracle_trie *t);
 
 /* Is `key` (len labels) a key of the trie?  (reference LoudsTrie::lookup) */
 int oracle_lookup(const oracle_trie *t, const uint32_t *key, uint32_t len);
+/* Key id of `key` (reference LoudsTrie::lookup: the rank of its terminal node
+ * among terminal nodes), or -1 if it is not a key. */
+int64_t oracle_lookup_id(const oracle_trie *t, const uint32_t *key, uint32_t len);
 
 /*
  * One search request.  Rows are topk_id/topk_logp[L][K] row-major.

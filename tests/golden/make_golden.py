@@ -19,11 +19,19 @@ Fixtures (JSON):
                 hand-built tries and requests covering links, internal link
                 nodes, terminal link nodes, thresholds, ties, duplicate ids,
                 unsorted rows and zero-width beams.
+  lookup_c1.json
+                key ids the reference's own lookup tool (tools/marisa-lookup.cc,
+                built by oracle/ref.mk) reports on the config-1 trie for keys,
+                prefixes of keys and random sequences (-1: not a key).
 The reference never runs on the GPU box; only these files travel.
+
+    python tests/golden/make_golden.py           # all fixtures
+    python tests/golden/make_golden.py lookup    # lookup_c1.json only
 """
 import hashlib
 import json
 import os
+import subprocess
 import sys
 
 import numpy as np
@@ -64,6 +72,38 @@ def format_cases():
     cases.append(("empty-key", [[]]))
     cases.append(("duplicates", [[5], [5], [5, 6], [5, 6], [9, 9, 9]]))
     return cases
+
+
+def c1_reference_trie():
+    import flashtrie_ref as ref
+    cfg = W.CONFIGS[1]
+    tok, off = W.gen_keys(cfg["keys"], cfg["vocab"], cfg["len_lo"], cfg["len_hi"], cfg["zipf"], seed=1)
+    t = ref.Trie()
+    t.build(token_rows=W.key_rows(tok, off))
+    path = "/tmp/golden_c1.bin"
+    t.save(path)
+    return t, tok, off, path
+
+
+def lookup_golden(tok, off, path):
+    rng = np.random.default_rng(17)
+    n = len(off) - 1
+    queries = []
+    for i in rng.choice(n, size=300, replace=False):
+        key = tok[off[i]:off[i + 1]].tolist()
+        queries.append(key)
+        if len(key) > 1:
+            queries.append(key[:int(rng.integers(1, len(key)))])  # a prefix: a key or not
+    for _ in range(100):
+        queries.append(rng.integers(0, W.CONFIGS[1]["vocab"], size=int(rng.integers(1, 6))).tolist())
+    tool = os.path.join(REPO, "oracle", "_ref", "marisa-lookup")
+    inp = "".join(" ".join(str(x) for x in q) + "\n" for q in queries)
+    res = subprocess.run([tool, path], input=inp, capture_output=True, text=True, check=True,
+                         env=dict(os.environ, MARISA_MANAGED_ALLOC="0"))
+    ids = [int(line.split("\t")[0]) for line in res.stdout.splitlines()]
+    assert len(ids) == len(queries)
+    with open(os.path.join(HERE, "lookup_c1.json"), "w") as f:
+        json.dump({"trie_sha256": file_sha(path), "queries": queries, "ids": ids}, f)
 
 
 def main():
@@ -149,4 +189,10 @@ def main():
 
 
 if __name__ == "__main__":
-    main()
+    if sys.argv[1:] == ["lookup"]:
+        _, tok, off, path = c1_reference_trie()
+        lookup_golden(tok, off, path)
+    else:
+        main()
+        _, tok, off, path = c1_reference_trie()
+        lookup_golden(tok, off, path)

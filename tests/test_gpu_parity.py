@@ -202,7 +202,7 @@ def test_device_entry_point_matches_host(ft, c1):
         _fields_ = [("n", ctypes.c_uint32), ("num_outpos", ctypes.c_uint32), ("topk", ctypes.c_uint32),
                     ("out_capacity", ctypes.c_uint32)] + [(f, ctypes.c_void_p) for f in
                                                           ("beams", "topk_id", "topk_logp", "out_count", "out_lpn",
-                                                           "out_len", "out_tok")]
+                                                           "out_len", "out_tok", "out_key")]
 
     dev = torch.device("cuda:0")
     d_beams = torch.from_numpy(beams.astype(np.int32)).to(dev)

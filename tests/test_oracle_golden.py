@@ -79,3 +79,16 @@ def test_oracle_matches_reference_cpu_hand(built, tmp_path):
         assert r["ref_invalid"] or r["early_exit"] or st.ties_at_cut > 0, r
     assert exact > len(g["requests"]) // 2
     print("hand: %d identical, %d explained" % (exact, explained))
+
+
+def test_oracle_key_ids_match_reference_lookup(c1_trie):
+    """Key ids (rank of the terminal node) against the reference's own lookup
+    tool on the same trie bytes: keys, prefixes of keys, random sequences."""
+    from oracle.oracle import OracleTrie
+    tok, off, path, g = c1_trie
+    lk = load_json("lookup_c1.json")
+    assert lk["trie_sha256"] == g["trie_sha256"]
+    o = OracleTrie(path)
+    got = [o.lookup_id(q) for q in lk["queries"]]
+    assert got == lk["ids"]
+    assert sum(i >= 0 for i in got) > 300

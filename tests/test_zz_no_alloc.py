@@ -31,7 +31,7 @@ class Batch(ctypes.Structure):
     _fields_ = [("n", ctypes.c_uint32), ("num_outpos", ctypes.c_uint32), ("topk", ctypes.c_uint32),
                 ("out_capacity", ctypes.c_uint32)] + [(f, ctypes.c_void_p) for f in
                                                       ("beams", "topk_id", "topk_logp", "out_count", "out_lpn",
-                                                       "out_len", "out_tok")]
+                                                       "out_len", "out_tok", "out_key")]
 
 
 def test_no_alloc_entry_point_matches_allocating_one(built, tmp_path):
