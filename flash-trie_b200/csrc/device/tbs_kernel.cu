@@ -1,15 +1,15 @@
-// Trie-constrained beam search kernels for sm_100a.
+// Trie-constrained beam search kernel for sm_100a.
 //
 // A request is searched by one thread-block cluster ("team") of 1 to 16 CTAs
 // that stays on the request for all its steps (persistent grid, requests
-// strided over teams).  Team-wide counters and the merged radix histogram live
-// in the shared memory of the team's rank-0 CTA and are updated with
-// distributed-shared-memory atomics; the phases of a step are separated by
-// hardware cluster barriers.  The reference launches one cooperative grid per
-// request and separates each step's expansion, pruning and history save with
-// 2-3 grid-wide syncs (lib/marisa/grimoire/trie/tbs-kernels.cu:476-594).
-// Small batches use large teams (latency), large batches 1-CTA teams
-// (throughput).
+// strided over teams).  Team counters live in the shared memory of the team's
+// rank-0 CTA and are updated with distributed-shared-memory atomics; radix
+// histograms stay in each CTA's own shared memory and are read remotely; the
+// phases of a step are separated by hardware cluster barriers.  The reference
+// launches one cooperative grid per request and separates each step's
+// expansion, pruning and history save with 2-3 grid-wide syncs
+// (lib/marisa/grimoire/trie/tbs-kernels.cu:476-594).  Small batches use large
+// teams (latency), large batches one-CTA teams (throughput).
 //
 // Per step t of a request:
 //   1. every CTA stages row t (ids ascending, log-probs, original columns)
@@ -19,22 +19,23 @@
 //      - in-link beams, one thread each: the next tail cell is the only
 //        allowed token; look it up in the sorted row (tbs-kernels.cu:324-371);
 //      - branching beams: a task table of (parent, 128 items) drained by all
-//        warps of the team; an item is a child whose label is looked up in the
-//        row (small fan-out), or a proposal that probes the parent's hash
-//        table (large fan-out) or binary-searches its child labels
-//        (tbs-kernels.cu:210-322); found children ("hits") are resolved in one
-//        bulk round that gathers their flags and link offsets;
+//        warps of the team; an item is a child whose record is loaded and its
+//        label looked up in the row (small fan-out), or a proposal that probes
+//        the parent's hash table (large fan-out) or binary-searches its child
+//        labels (tbs-kernels.cu:210-322), then loads what it found;
 //      - thresholds: logp > token_threshold and score + logp > sent_threshold,
 //        compared in f64 (tbs-kernels.cu:229-231);
 //      - children go to the step's candidate list and, when they end a key,
-//        to the result pool;
+//        to the result pool (one warp-wide reservation per task);
 //   3. select: exact top-beams[t] of the candidates in the pinned order
 //      (logp_norm, node, depth, score), an 11-bit MSD radix select over the
 //      192-bit key starting after the bits all candidates share; survivors
 //      become the next step's beams and append (parent, token) history;
-//   4. trim the result pool to the final beam the same way.
+//   4. trim the result pool to the final beam the same way when the next
+//      step could overflow it.
 // After the last step the pool is sorted and written ascending with each
-// sequence rebuilt from the history (tbs-kernels.cu:393-474).
+// sequence rebuilt from the history (tbs-kernels.cu:393-474), and with each
+// result's key id when asked.
 #include <cooperative_groups.h>
 #include <cooperative_groups/reduce.h>
 
