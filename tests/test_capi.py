@@ -39,3 +39,18 @@ def test_host_entry_points_without_gpu(built, tmp_path):
     assert lib.ft_trie_load(h, b"/nonexistent/trie.bin") == -9  # FT_ERR_IO
     assert b"IO_ERROR" in lib.ft_last_error()
     lib.ft_trie_destroy(h)
+
+
+def test_device_api_rejects_host_tensors(built):
+    """flashtrie_device validates its inputs before touching a device."""
+    import pytest
+    import torch
+    import flashtrie
+    import flashtrie_device as fd
+    t = flashtrie.Trie()
+    t.build(token_rows=[[1, 2], [1, 3]])
+    beams = torch.ones((1, 2), dtype=torch.int32)
+    ids = torch.zeros((1, 2, 4), dtype=torch.int32)
+    lp = torch.zeros((1, 2, 4), dtype=torch.float32)
+    with pytest.raises(TypeError):
+        fd.bs_tbs_device(t, beams, ids, lp, -10.0, -40.0, 1.0, False)
