@@ -1,0 +1,115 @@
+"""Parity at the configurations' own sizes.
+
+Config 2 is searched at its full size (10M keys, V=500k, K=256, L=16, beam
+100) and compared with the oracle request by request.  Configs 3 and 5 keep
+their request shapes (K=1000, L=20/24, beam 1000, V=2.2M; config 5 with
+early exit and 30% off-trie requests) on a 12M-key trie of their key
+distribution; FT_FULLSIZE=1 adds config 3 at its full 200M keys.
+
+Besides the direct comparison, every result of every request is checked
+through properties that hold at any size: at most beams[L-1] results, in
+ascending logp_norm, distinct, each a key of the trie with the key id the
+oracle's lookup gives, each token proposed at its position above the token
+threshold, every prefix score above the sentence threshold, and the score
+recomputed from the proposals (f32 log-probabilities summed in f64, times
+(6/(5+len))^length_norm) equal to the reported one.
+"""
+import os
+
+import numpy as np
+import pytest
+
+import workload as W
+from helpers import same_result
+
+pytestmark = pytest.mark.gpu
+
+TT, ST, LN = W.TOKEN_LOGP_THRESHOLD, W.SENT_LOGP_THRESHOLD, W.LENGTH_NORM
+
+
+def _build(tmp_path_factory, cfg_id, n_keys, name):
+    import flashtrie
+    cfg = dict(W.CONFIGS[cfg_id], keys=n_keys)
+    tok, off = W.gen_keys_torch(n_keys, cfg["vocab"], cfg["len_lo"], cfg["len_hi"], cfg["zipf"], seed=cfg_id,
+                                device="cuda")
+    t = flashtrie.Trie()
+    t.build_flat(tok, off)
+    path = str(tmp_path_factory.mktemp(name) / "trie.bin")
+    t.save(path)
+    del t
+    return path, tok, off, cfg
+
+
+def check_properties(o, beams, ids, lp, sents, lpns, keys):
+    """The size-independent properties of one request's results."""
+    L = ids.shape[0]
+    final_beam = int(beams[-1])
+    assert len(sents) == len(lpns) == len(keys) and len(sents) <= final_beam
+    assert all(a <= b for a, b in zip(lpns, lpns[1:])), "not ascending"
+    assert len({tuple(s) for s in sents}) == len(sents), "duplicate results"
+    for s, lpn, key in zip(sents, lpns, keys):
+        assert 1 <= len(s) <= L
+        score = 0.0
+        for t, tok in enumerate(s):
+            cols = np.flatnonzero(ids[t] == tok)
+            assert cols.size, "token %d not proposed at position %d" % (tok, t)
+            v = float(lp[t][cols[0]])
+            assert v > TT
+            score += v
+            assert score > ST
+        f = (6.0 / (5.0 + len(s))) ** LN
+        assert lpn == pytest.approx(score * f, rel=1e-12, abs=0.0)
+        assert key != 0xFFFFFFFF and o.lookup_id(s) == key, "result is not the key it claims"
+
+
+def _search(t, beams, ids, lp, early_exit):
+    import flashtrie
+    n = beams.shape[0]
+    return flashtrie.bs_tbs_gpu(t, n, beams, ids, lp, TT, ST, LN, early_exit, return_key_ids=True)
+
+
+def _run(path, tok, off, cfg, cfg_id, n_req, n_direct):
+    import flashtrie
+    from oracle.oracle import OracleTrie
+    beams, ids, lp = W.gen_requests(cfg_id, tok, off, n_req, cfg=cfg)
+    t = flashtrie.Trie()
+    t.load(path)
+    t.init_tbs_gpu(n_req, max_num_topk=cfg["K"], max_num_outpos=cfg["L"], max_num_out_beams=cfg["beam"])
+    sents, lpns, _, _, keys = _search(t, beams, ids, lp, cfg["early_exit"])
+    o = OracleTrie(path)
+    total = 0
+    for i in range(n_req):
+        check_properties(o, beams[i], ids[i], lp[i], sents[i], lpns[i], keys[i])
+        total += len(sents[i])
+        if i < n_direct:
+            o_s, o_l = o.tbs(beams[i], ids[i], lp[i], TT, ST, LN, cfg["early_exit"])
+            assert same_result(sents[i], lpns[i], o_s, o_l), i
+    # One request searched alone returns what it returned inside the batch.
+    one = _search(t, beams[:1], ids[:1], lp[:1], cfg["early_exit"])
+    assert one[0][0] == sents[0] and one[1][0] == lpns[0] and one[4][0] == keys[0]
+    return total
+
+
+@pytest.fixture(scope="module")
+def c2_full(tmp_path_factory, built):
+    return _build(tmp_path_factory, 2, W.CONFIGS[2]["keys"], "c2")
+
+
+def test_config2_full_size_matches_oracle(c2_full):
+    path, tok, off, cfg = c2_full
+    total = _run(path, tok, off, cfg, 2, n_req=48, n_direct=12)
+    assert total > 48 * 10  # the requests do find many keys
+
+
+@pytest.mark.parametrize("cfg_id", [3, 5])
+def test_config_shapes_at_12m_keys(tmp_path_factory, built, cfg_id):
+    path, tok, off, cfg = _build(tmp_path_factory, cfg_id, 12_000_000, "c%d" % cfg_id)
+    total = _run(path, tok, off, cfg, cfg_id, n_req=24, n_direct=8)
+    assert total > 0
+
+
+@pytest.mark.skipif(os.environ.get("FT_FULLSIZE") != "1", reason="200M-key trie; set FT_FULLSIZE=1")
+def test_config3_full_size_matches_oracle(tmp_path_factory, built):
+    path, tok, off, cfg = _build(tmp_path_factory, 3, W.CONFIGS[3]["keys"], "c3full")
+    total = _run(path, tok, off, cfg, 3, n_req=16, n_direct=16)
+    assert total > 16 * 10
