@@ -795,6 +795,13 @@ __device__ void expand_branch(const Ctx &c, const BranchTable &bt) {
   }
 }
 
+// Counts `key` in its bin of the current pass if it matches the prefix.
+__device__ __forceinline__ void hist_add(const Key3 &key, const Key3 &P, const Key3 &M, int from_top, int width,
+                                         uint32_t *hist) {
+  if ((key.w[0] & M.w[0]) == P.w[0] && (key.w[1] & M.w[1]) == P.w[1] && (key.w[2] & M.w[2]) == P.w[2])
+    atomicAdd(&hist[key_bits(key, from_top, width)], 1u);
+}
+
 // ------------------------------------------------------------- selection
 // Exact top-k threshold over n candidates by the 192-bit key, computed by the
 // whole team with one cluster barrier per radix pass.  Each CTA histograms
@@ -808,12 +815,12 @@ __device__ void expand_branch(const Ctx &c, const BranchTable &bt) {
 // to those of common_hi << 32).  On return every CTA's LocalState holds the
 // threshold: with sel_ge every key >= sel_prefix is taken (exactly k of them),
 // otherwise keys > sel_prefix plus sel_rem keys equal to it.
-template <bool kPoolKeys>
-__device__ void team_radix_select(const Ctx &c, const Cand *v, uint32_t n, uint32_t k, uint32_t depth_const,
-                                  int start, uint32_t common_hi) {
+// `add_keys(P, M, from_top, width, hist)` histograms (hist_add) this
+// thread's keys, from memory or from registers.
+template <class AddKeys>
+__device__ void team_radix_select(const Ctx &c, uint32_t k, int start, uint32_t common_hi, AddKeys &&add_keys) {
   LocalState *S = c.S;
   const uint32_t cs = c.cs;
-  const double *factor = c.p->factor;
   cg::cluster_group cluster = cg::this_cluster();
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __syncthreads();  // this CTA may still be testing keys against the previous threshold
@@ -825,8 +832,6 @@ __device__ void team_radix_select(const Ctx &c, const Cand *v, uint32_t n, uint3
     S->sel_ge = 0;
   }
   __syncthreads();
-  const uint32_t max_depth = c.step + 1;
-  const double fac_const = factor[depth_const];
   for (int from_top = start; from_top < kKeyBits; from_top += kRadixBits) {
     const int width = min(kRadixBits, kKeyBits - from_top);
     const uint32_t buf = S->pass & 1u;
@@ -835,13 +840,7 @@ __device__ void team_radix_select(const Ctx &c, const Cand *v, uint32_t n, uint3
     for (int b = threadIdx.x; b < kRadixBins; b += blockDim.x) hist[b] = 0;
     const Key3 P = S->sel_prefix, M = S->sel_mask;
     __syncthreads();
-    for (uint32_t i = c.gtid(); i < n; i += c.gthreads()) {
-      const Cand cv = ld_cand(v + i);
-      const uint32_t depth = kPoolKeys ? min(cv.aux, max_depth) : depth_const;
-      const Key3 key = cand_key(cv, kPoolKeys ? factor[depth] : fac_const, depth);
-      if ((key.w[0] & M.w[0]) == P.w[0] && (key.w[1] & M.w[1]) == P.w[1] && (key.w[2] & M.w[2]) == P.w[2])
-        atomicAdd(&hist[key_bits(key, from_top, width)], 1u);
-    }
+    add_keys(P, M, from_top, width, hist);
     __syncthreads();
     {
       // Super-bin sums: thread i sums bins 4i..4i+3; 8 lanes make a super-bin.
@@ -953,47 +952,85 @@ __device__ __forceinline__ int common_bits(uint32_t lo, uint32_t hi) {
   return lo == hi ? 32 : __clz((int)(lo ^ hi));
 }
 
+// Appends a selected candidate to the beams of step t+1 and its history.
+__device__ __forceinline__ void take_beam(const Ctx &c, const Cand &v, uint32_t k, Beam *out_beams, Hist *hist) {
+  if (append_slot(&c.cnt->n_sel) >= k) {
+    atomicOr(c.p->status, kStatusSelection);
+    return;
+  }
+  // In-link beams fill the buffer from the front, branching beams from the
+  // back; the capped total keeps the two from overlapping.
+  const uint32_t beam_cap = c.p->beam_cap;
+  uint32_t idx;
+  if (rec_flags(v.dw) & kNodeFlagLink) {
+    idx = append_slot(&c.cnt->n_in_new);
+  } else {
+    idx = beam_cap - 1 - append_slot(&c.cnt->n_br_new);
+  }
+  Beam b;
+  b.score = v.score;
+  b.node = v.node;
+  b.off = v.aux;
+  b.c0 = v.c0;
+  b.dw = v.dw;
+  out_beams[idx] = b;
+  hist[idx] = Hist{v.parent, v.token};
+}
+
 // Makes the selected candidates the beams of step t+1.
 __device__ void materialize_next(const Ctx &c, uint32_t n, uint32_t k, Beam *out_beams) {
   const uint32_t depth = c.step + 1;
   const double f = c.p->factor[depth];
-  const bool all = n <= k;
   if (k == 0) return;
+  const Cand *next = c.slot.next;
+  Hist *hist = c.slot.hist + (uint64_t)depth * c.p->beam_cap;
+  const int start = common_bits(c.S->key_min, c.S->key_max);
+  if (n > k && n <= c.gthreads()) {
+    // One candidate per thread at most: it stays in registers through every
+    // radix pass and the final test, so nothing is read twice.
+    const uint32_t i = c.gtid();
+    const bool have = i < n;
+    Cand v = {};
+    Key3 key = {};
+    if (have) {
+      v = ld_cand(next + i);
+      key = cand_key(v, f, depth);
+    }
+    team_radix_select(c, k, start, c.S->key_min,
+                      [&](const Key3 &P, const Key3 &M, int from_top, int width, uint32_t *h) {
+                        if (have) hist_add(key, P, M, from_top, width, h);
+                      });
+    if (have && is_selected(c, key, &c.cnt->eq_taken)) take_beam(c, v, k, out_beams, hist);
+    return;
+  }
+  const bool all = n <= k;
   if (!all)
-    team_radix_select<false>(c, c.slot.next, n, k, depth, common_bits(c.S->key_min, c.S->key_max), c.S->key_min);
-  const uint32_t beam_cap = c.p->beam_cap;
-  Hist *hist = c.slot.hist + (uint64_t)depth * beam_cap;
+    team_radix_select(c, k, start, c.S->key_min,
+                      [&](const Key3 &P, const Key3 &M, int from_top, int width, uint32_t *h) {
+                        for (uint32_t i = c.gtid(); i < n; i += c.gthreads())
+                          hist_add(cand_key(ld_cand(next + i), f, depth), P, M, from_top, width, h);
+                      });
   for (uint32_t i = c.gtid(); i < n; i += c.gthreads()) {
-    const Cand v = ld_cand(c.slot.next + i);
+    const Cand v = ld_cand(next + i);
     if (!all && !is_selected(c, cand_key(v, f, depth), &c.cnt->eq_taken)) continue;
-    if (append_slot(&c.cnt->n_sel) >= k) {
-      atomicOr(c.p->status, kStatusSelection);
-      continue;
-    }
-    // In-link beams fill the buffer from the front, branching beams from the
-    // back; the capped total keeps the two from overlapping.
-    uint32_t idx;
-    if (rec_flags(v.dw) & kNodeFlagLink) {
-      idx = append_slot(&c.cnt->n_in_new);
-    } else {
-      idx = beam_cap - 1 - append_slot(&c.cnt->n_br_new);
-    }
-    Beam b;
-    b.score = v.score;
-    b.node = v.node;
-    b.off = v.aux;
-    b.c0 = v.c0;
-    b.dw = v.dw;
-    out_beams[idx] = b;
-    hist[idx] = Hist{v.parent, v.token};
+    take_beam(c, v, k, out_beams, hist);
   }
 }
 
 // Writes the best k of the n pool entries to pool_tmp (the team's
 // n_compact counts them).
 __device__ void trim_pool(const Ctx &c, uint32_t n, uint32_t k) {
-  team_radix_select<true>(c, c.slot.pool, n, k, 0, common_bits(c.S->pool_key_min, c.S->pool_key_max),
-                          c.S->pool_key_min);
+  const Cand *pool = c.slot.pool;
+  const double *factor = c.p->factor;
+  const uint32_t max_depth = c.step + 1;
+  team_radix_select(c, k, common_bits(c.S->pool_key_min, c.S->pool_key_max), c.S->pool_key_min,
+                    [&](const Key3 &P, const Key3 &M, int from_top, int width, uint32_t *h) {
+                      for (uint32_t i = c.gtid(); i < n; i += c.gthreads()) {
+                        const Cand cv = ld_cand(pool + i);
+                        const uint32_t d = min(cv.aux, max_depth);
+                        hist_add(cand_key(cv, factor[d], d), P, M, from_top, width, h);
+                      }
+                    });
   for (uint32_t i = c.gtid(); i < n; i += c.gthreads()) {
     const Cand v = ld_cand(c.slot.pool + i);
     if (v.aux == 0 || v.aux > c.step + 1) {
