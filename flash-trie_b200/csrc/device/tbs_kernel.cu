@@ -487,6 +487,31 @@ __device__ __forceinline__ uint32_t warp_reserve(uint32_t *counter, uint32_t n) 
   return __shfl_sync(0xFFFFFFFFu, base, 0) + inc - n;
 }
 
+// Two reservations at once (called by all 32 lanes): lanes 0 and 1 issue
+// their atomics in the same instruction, so the warp waits for one round
+// trip instead of two.
+__device__ __forceinline__ void warp_reserve2(uint32_t *ca, uint32_t na, uint32_t *cb, uint32_t nb, uint32_t &ba,
+                                              uint32_t &bb) {
+  const uint32_t lane = threadIdx.x & 31;
+  uint32_t ia = na, ib = nb;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t ya = __shfl_up_sync(0xFFFFFFFFu, ia, o);
+    const uint32_t yb = __shfl_up_sync(0xFFFFFFFFu, ib, o);
+    if (lane >= (uint32_t)o) {
+      ia += ya;
+      ib += yb;
+    }
+  }
+  const uint32_t ta = __shfl_sync(0xFFFFFFFFu, ia, 31), tb = __shfl_sync(0xFFFFFFFFu, ib, 31);
+  uint32_t *ctr = lane == 0 ? ca : cb;
+  const uint32_t tot = lane == 0 ? ta : tb;
+  uint32_t base = 0;
+  if (lane < 2 && tot) base = atomicAdd(ctr, tot);
+  ba = __shfl_sync(0xFFFFFFFFu, base, 0) + ia - na;
+  bb = __shfl_sync(0xFFFFFFFFu, base, 1) + ib - nb;
+}
+
 __device__ __forceinline__ void write_next(const Ctx &c, uint32_t idx, double score, uint32_t node, uint32_t aux,
                                            uint32_t parent, uint32_t token, uint32_t c0, uint32_t dw) {
   const uint32_t k32 = (uint32_t)(orderable(score * c.f_next) >> 32);
@@ -544,8 +569,8 @@ __device__ __forceinline__ void emit_task(const Ctx &c, double pscore, uint32_t 
     nn += nx;
     np += pl;
   });
-  uint32_t bn = warp_reserve(&c.cnt->n_next, nn);
-  uint32_t bp = warp_reserve(&c.T->pool_end, np);
+  uint32_t bn, bp;
+  warp_reserve2(&c.cnt->n_next, nn, &c.T->pool_end, np, bn, bp);
   if (nn + np == 0) return;
   pairs([&](uint32_t k, uint32_t m) {
     const double lp = (double)c.row.lp[m];
@@ -837,9 +862,7 @@ __device__ void team_radix_select(const Ctx &c, uint32_t k, int start, uint32_t 
     const uint32_t buf = S->pass & 1u;
     uint32_t *hist = S->hist[buf];
     uint32_t *super = S->super[buf];
-    for (int b = threadIdx.x; b < kRadixBins; b += blockDim.x) hist[b] = 0;
     const Key3 P = S->sel_prefix, M = S->sel_mask;
-    __syncthreads();
     add_keys(P, M, from_top, width, hist);
     __syncthreads();
     {
@@ -852,6 +875,13 @@ __device__ void team_radix_select(const Ctx &c, uint32_t k, int start, uint32_t 
       if ((threadIdx.x & 7) == 0) super[threadIdx.x >> 3] = s4;
     }
     team_sync(cs);
+    {
+      // The other buffer was last read (over DSMEM) before the barrier above:
+      // clear it for the next pass, which the barriers below order before
+      // that pass's adds.
+      uint32_t *other = S->hist[buf ^ 1u];
+      for (int b = threadIdx.x; b < kRadixBins; b += blockDim.x) other[b] = 0;
+    }
     uint32_t *part = S->part;
     if (warp < cs) {
       const uint2 pv = *reinterpret_cast<const uint2 *>(cluster.map_shared_rank(super, warp) + 2 * lane);
@@ -862,10 +892,14 @@ __device__ void team_radix_select(const Ctx &c, uint32_t k, int start, uint32_t 
       const uint32_t rem = S->sel_rem;
       // Lane l holds super-bins 63-2l (upper) and 62-2l (lower).
       uint32_t hi_s = 0, lo_s = 0;
-      for (uint32_t r = 0; r < cs; ++r) {
-        const uint2 pv = *reinterpret_cast<const uint2 *>(part + r * kSuperBins + kSuperBins - 2 - 2 * lane);
-        hi_s += pv.y;
-        lo_s += pv.x;
+      // Unrolled so that the team's loads are all in flight at once.
+#pragma unroll
+      for (uint32_t r = 0; r < kMaxTeam; ++r) {
+        if (r < cs) {
+          const uint2 pv = *reinterpret_cast<const uint2 *>(part + r * kSuperBins + kSuperBins - 2 - 2 * lane);
+          hi_s += pv.y;
+          lo_s += pv.x;
+        }
       }
       uint32_t inc = hi_s + lo_s;
 #pragma unroll
@@ -900,7 +934,9 @@ __device__ void team_radix_select(const Ctx &c, uint32_t k, int start, uint32_t 
       if (sb != 0xFFFFFFFFu) {
         // Lane l holds bin sb*32 + 31 - l (descending).
         uint32_t bv = 0;
-        for (uint32_t r = 0; r < cs; ++r) bv += part[r * 32 + lane];
+#pragma unroll
+        for (uint32_t r = 0; r < kMaxTeam; ++r)
+          if (r < cs) bv += part[r * 32 + lane];
         uint32_t binc = bv;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -953,20 +989,38 @@ __device__ __forceinline__ int common_bits(uint32_t lo, uint32_t hi) {
 }
 
 // Appends a selected candidate to the beams of step t+1 and its history.
+// In-link beams fill the buffer from the front, branching beams from the
+// back; the capped total keeps the two from overlapping.  The converged
+// threads reserve together: one thread issues the three counter atomics back
+// to back (one round trip) for all of them.
 __device__ __forceinline__ void take_beam(const Ctx &c, const Cand &v, uint32_t k, Beam *out_beams, Hist *hist) {
-  if (append_slot(&c.cnt->n_sel) >= k) {
+  const uint32_t act = __activemask();
+  const uint32_t lane = threadIdx.x & 31;
+  const bool link = rec_flags(v.dw) & kNodeFlagLink;
+  const uint32_t m_in = __ballot_sync(act, link);
+  const uint32_t m_br = act & ~m_in;
+  const uint32_t leader = __ffs(act) - 1;
+  uint32_t b_sel = 0, b_in = 0, b_br = 0;
+  if (lane == leader) {
+    b_sel = atomicAdd(&c.cnt->n_sel, (uint32_t)__popc(act));
+    if (m_in) b_in = atomicAdd(&c.cnt->n_in_new, (uint32_t)__popc(m_in));
+    if (m_br) b_br = atomicAdd(&c.cnt->n_br_new, (uint32_t)__popc(m_br));
+  }
+  b_sel = __shfl_sync(act, b_sel, leader);
+  b_in = __shfl_sync(act, b_in, leader);
+  b_br = __shfl_sync(act, b_br, leader);
+  const uint32_t below = (1u << lane) - 1u;
+  if (b_sel + (uint32_t)__popc(act & below) >= k) {
     atomicOr(c.p->status, kStatusSelection);
     return;
   }
-  // In-link beams fill the buffer from the front, branching beams from the
-  // back; the capped total keeps the two from overlapping.
   const uint32_t beam_cap = c.p->beam_cap;
-  uint32_t idx;
-  if (rec_flags(v.dw) & kNodeFlagLink) {
-    idx = append_slot(&c.cnt->n_in_new);
-  } else {
-    idx = beam_cap - 1 - append_slot(&c.cnt->n_br_new);
+  const uint32_t j = link ? b_in + __popc(m_in & below) : b_br + __popc(m_br & below);
+  if (j >= beam_cap) {
+    atomicOr(c.p->status, kStatusSelection);
+    return;
   }
+  const uint32_t idx = link ? j : beam_cap - 1 - j;
   Beam b;
   b.score = v.score;
   b.node = v.node;
@@ -1258,6 +1312,9 @@ __device__ void search_request(const SearchParams &p, uint32_t req, const SlotVi
     T->removed = 0;
   }
   if (threadIdx.x == 0) S->pass = 0;
+  // Both histogram buffers start clear; afterwards each pass clears the
+  // buffer of the pass after it (team_radix_select).
+  for (uint32_t b = threadIdx.x; b < 2 * kRadixBins; b += blockDim.x) (&S->hist[0][0])[b] = 0;
   RowView row;
   row.id = reinterpret_cast<uint32_t *>(dyn);
   row.lp = reinterpret_cast<float *>(dyn + sizeof(uint32_t) * K);
