@@ -58,21 +58,20 @@ Engine::Engine(std::shared_ptr<DeviceTrie> trie, const EngineLimits &lim) : trie
     }
     d_slots_ = (SlotView *)dalloc(sizeof(SlotView) * n_slots_);
     CUDA_TRY(cudaMemcpy(d_slots_, slots.data(), sizeof(SlotView) * n_slots_, cudaMemcpyHostToDevice));
-    d_status_ = (uint32_t *)dalloc(16);
-    CUDA_TRY(cudaMemset(d_status_, 0, 16));
     d_status_dev_ = (uint32_t *)dalloc(16);
     CUDA_TRY(cudaMemset(d_status_dev_, 0, 16));
     d_debug_ = (uint32_t *)dalloc(64);
     CUDA_TRY(cudaMemset(d_debug_, 0, 64));
 
+    // One staging buffer per side: a call's inputs, then its outputs (whose
+    // first 16 bytes, the status and token-total words, travel with the
+    // inputs so that the one host-to-device copy also clears them).
     in_bytes_ = align16(sizeof(ReqMeta) * NB) + align16(8 * (L + 1)) + align16(4 * NB * L) + 2 * align16(4 * NB * L * K);
-    d_in_ = (uint8_t *)dalloc(in_bytes_);
-    CUDA_TRY(cudaMallocHost(&h_in_, in_bytes_));
     out_bytes_ = 16 + align16(4 * NB) + align16(8 * 5 * NB) + align16(8 * NB * B) + 2 * align16(4 * NB * B) +
                  align16(8 * NB) +
                  align16(4 * NB * B * L);
-    d_out_ = (uint8_t *)dalloc(out_bytes_);
-    CUDA_TRY(cudaMallocHost(&h_out_, out_bytes_));
+    d_io_ = (uint8_t *)dalloc(in_bytes_ + out_bytes_);
+    CUDA_TRY(cudaMallocHost(&h_io_, in_bytes_ + out_bytes_));
     dmeta_bytes_ = align16(sizeof(ReqMeta) * NB) + align16(8 * (L + 1));
     d_dmeta_ = (uint8_t *)dalloc(dmeta_bytes_);
     CUDA_TRY(cudaMallocHost(&h_dmeta_, dmeta_bytes_));
@@ -93,12 +92,11 @@ void Engine::release() {
   if (stream_) cudaStreamSynchronize(stream_);
   for (auto &a : allocs_) cudaFree(a.p);
   allocs_.clear();
-  if (h_in_) cudaFreeHost(h_in_);
-  if (h_out_) cudaFreeHost(h_out_);
+  if (h_io_) cudaFreeHost(h_io_);
   if (h_dmeta_) cudaFreeHost(h_dmeta_);
   if (dmeta_done_) cudaEventDestroy(dmeta_done_);
   if (stream_) cudaStreamDestroy(stream_);
-  h_in_ = h_out_ = h_dmeta_ = nullptr;
+  h_io_ = h_dmeta_ = nullptr;
   stream_ = nullptr;
   dmeta_done_ = nullptr;
   if (prev >= 0) cudaSetDevice(prev);
@@ -132,8 +130,7 @@ void Engine::fill_params(SearchParams &sp, const ft_search_params &prm, uint32_t
   sp.token_threshold = (double)prm.token_logp_threshold;
   sp.sent_threshold = prm.sent_logp_threshold;
   sp.early_exit = prm.early_exit ? 1 : 0;
-  sp.status = d_status_;
-  sp.debug = d_debug_;
+  sp.debug = d_debug_;  // the caller sets sp.status
 }
 
 void Engine::search_host(const ft_request *reqs, uint32_t n, const ft_search_params &prm, ft_result *out) {
@@ -164,11 +161,11 @@ void Engine::search_host(const ft_request *reqs, uint32_t n, const ft_search_par
   const size_t o_meta = 0, o_fac = align16(sizeof(ReqMeta) * n), o_beams = o_fac + align16(8 * (max_L + 1)),
                o_ids = o_beams + align16(4 * sum_L), o_lp = o_ids + align16(4 * sum_LK),
                in_used = o_lp + align16(4 * sum_LK);
-  ReqMeta *meta = reinterpret_cast<ReqMeta *>(h_in_ + o_meta);
-  fill_factor(reinterpret_cast<double *>(h_in_ + o_fac), max_L, prm.length_norm);
-  uint32_t *hb = reinterpret_cast<uint32_t *>(h_in_ + o_beams);
-  uint32_t *hid = reinterpret_cast<uint32_t *>(h_in_ + o_ids);
-  float *hlp = reinterpret_cast<float *>(h_in_ + o_lp);
+  ReqMeta *meta = reinterpret_cast<ReqMeta *>(h_io_ + o_meta);
+  fill_factor(reinterpret_cast<double *>(h_io_ + o_fac), max_L, prm.length_norm);
+  uint32_t *hb = reinterpret_cast<uint32_t *>(h_io_ + o_beams);
+  uint32_t *hid = reinterpret_cast<uint32_t *>(h_io_ + o_ids);
+  float *hlp = reinterpret_cast<float *>(h_io_ + o_lp);
   uint64_t bo = 0, ro = 0;
   for (uint32_t i = 0; i < n; ++i) {
     const ft_request &r = reqs[i];
@@ -188,11 +185,14 @@ void Engine::search_host(const ft_request *reqs, uint32_t n, const ft_search_par
       std::memcpy(hlp + meta[i].rows_off, r.topk_logp, 4 * lk);
     }
   }
-  CUDA_TRY(cudaMemcpyAsync(d_in_, h_in_, in_used, cudaMemcpyHostToDevice, stream_));
-
   // Output region [status, token total | count | phase | lpn | len | key | token base | tok] for
-  // this batch; tokens are written compactly (each request's at the base it reserves), so only
-  // the tokens actually produced need to come back.
+  // this batch, right after the inputs; tokens are written compactly (each request's at the base
+  // it reserves), so only the tokens actually produced need to come back.  The status and
+  // token-total words go down zeroed with the inputs.
+  uint8_t *const d_out = d_io_ + in_used, *const h_out = h_io_ + in_used;
+  std::memset(h_out, 0, 16);
+  CUDA_TRY(cudaMemcpyAsync(d_io_, h_io_, in_used + 16, cudaMemcpyHostToDevice, stream_));
+
   const uint32_t stride = max_L;
   bool want_keys = false;
   for (uint32_t i = 0; i < n; ++i) want_keys |= out[i].key_ids != nullptr;
@@ -200,44 +200,42 @@ void Engine::search_host(const ft_request *reqs, uint32_t n, const ft_search_par
                q_len = q_lpn + align16(8ull * n * cap), q_key = q_len + align16(4ull * n * cap),
                q_base = q_key + (want_keys ? align16(4ull * n * cap) : 0), q_tok = q_base + align16(8ull * n),
                tok_bytes_max = 4ull * n * cap * stride;
-  CUDA_TRY(cudaMemsetAsync(d_status_, 0, 4, stream_));
-  CUDA_TRY(cudaMemsetAsync(d_out_ + 8, 0, 8, stream_));
 
   SearchParams sp;
   fill_params(sp, prm, n);
-  sp.meta = reinterpret_cast<const ReqMeta *>(d_in_ + o_meta);
-  sp.factor = reinterpret_cast<const double *>(d_in_ + o_fac);
-  sp.beams = reinterpret_cast<const uint32_t *>(d_in_ + o_beams);
-  sp.topk_id = reinterpret_cast<const uint32_t *>(d_in_ + o_ids);
-  sp.topk_logp = reinterpret_cast<const float *>(d_in_ + o_lp);
+  sp.status = reinterpret_cast<uint32_t *>(d_out);
+  sp.meta = reinterpret_cast<const ReqMeta *>(d_io_ + o_meta);
+  sp.factor = reinterpret_cast<const double *>(d_io_ + o_fac);
+  sp.beams = reinterpret_cast<const uint32_t *>(d_io_ + o_beams);
+  sp.topk_id = reinterpret_cast<const uint32_t *>(d_io_ + o_ids);
+  sp.topk_logp = reinterpret_cast<const float *>(d_io_ + o_lp);
   sp.out_cap = cap;
   sp.out_stride = stride;
-  sp.out_count = reinterpret_cast<uint32_t *>(d_out_ + q_count);
-  sp.out_phase_ms = reinterpret_cast<double *>(d_out_ + q_phase);
-  sp.out_lpn = reinterpret_cast<double *>(d_out_ + q_lpn);
-  sp.out_len = reinterpret_cast<uint32_t *>(d_out_ + q_len);
-  sp.out_tok = reinterpret_cast<uint32_t *>(d_out_ + q_tok);
-  sp.out_key = want_keys ? reinterpret_cast<uint32_t *>(d_out_ + q_key) : nullptr;
-  sp.tok_total = reinterpret_cast<uint64_t *>(d_out_ + 8);
-  sp.out_tok_base = reinterpret_cast<uint64_t *>(d_out_ + q_base);
+  sp.out_count = reinterpret_cast<uint32_t *>(d_out + q_count);
+  sp.out_phase_ms = reinterpret_cast<double *>(d_out + q_phase);
+  sp.out_lpn = reinterpret_cast<double *>(d_out + q_lpn);
+  sp.out_len = reinterpret_cast<uint32_t *>(d_out + q_len);
+  sp.out_tok = reinterpret_cast<uint32_t *>(d_out + q_tok);
+  sp.out_key = want_keys ? reinterpret_cast<uint32_t *>(d_out + q_key) : nullptr;
+  sp.tok_total = reinterpret_cast<uint64_t *>(d_out + 8);
+  sp.out_tok_base = reinterpret_cast<uint64_t *>(d_out + q_base);
   const SearchLaunch plan = plan_search(n, smem_);
   const int grid = (int)std::min<uint32_t>(std::min<uint32_t>(n, n_slots_), (uint32_t)plan.max_teams);
   launch_search(sp, smem_, grid, stream_, plan);
-  CUDA_TRY(cudaMemcpyAsync(d_out_, d_status_, 4, cudaMemcpyDeviceToDevice, stream_));
   // Small batches: everything in one copy.  Large ones: the headers first,
   // then only the tokens produced.
   const bool two_phase = tok_bytes_max > kOneCopyTokenBytes;
-  CUDA_TRY(cudaMemcpyAsync(h_out_, d_out_, two_phase ? q_tok : q_tok + tok_bytes_max, cudaMemcpyDeviceToHost,
+  CUDA_TRY(cudaMemcpyAsync(h_out, d_out, two_phase ? q_tok : q_tok + tok_bytes_max, cudaMemcpyDeviceToHost,
                            stream_));
   CUDA_TRY(cudaStreamSynchronize(stream_));
-  const uint64_t tok_total = *reinterpret_cast<const uint64_t *>(h_out_ + 8);
+  const uint64_t tok_total = *reinterpret_cast<const uint64_t *>(h_out + 8);
   if (tok_total * 4 > tok_bytes_max) throw std::runtime_error("tbs: the search kernel reported an invalid token total");
   if (two_phase && tok_total) {
-    CUDA_TRY(cudaMemcpyAsync(h_out_ + q_tok, d_out_ + q_tok, 4 * tok_total, cudaMemcpyDeviceToHost, stream_));
+    CUDA_TRY(cudaMemcpyAsync(h_out + q_tok, d_out + q_tok, 4 * tok_total, cudaMemcpyDeviceToHost, stream_));
     CUDA_TRY(cudaStreamSynchronize(stream_));
   }
 
-  const uint32_t status = *reinterpret_cast<const uint32_t *>(h_out_);
+  const uint32_t status = *reinterpret_cast<const uint32_t *>(h_out);
   if (status != 0) {
     uint32_t dbg[8] = {0};
     CUDA_TRY(cudaMemcpy(dbg, d_debug_, sizeof(dbg), cudaMemcpyDeviceToHost));
@@ -246,13 +244,13 @@ void Engine::search_host(const ft_request *reqs, uint32_t n, const ft_search_par
     throw std::runtime_error("tbs: the search kernel reported a failed self-check (status " + std::to_string(status) +
                              ", detail " + d + ")");
   }
-  const uint32_t *hcount = reinterpret_cast<const uint32_t *>(h_out_ + q_count);
-  const double *hphase = reinterpret_cast<const double *>(h_out_ + q_phase);
-  const double *hlpn = reinterpret_cast<const double *>(h_out_ + q_lpn);
-  const uint32_t *hlen = reinterpret_cast<const uint32_t *>(h_out_ + q_len);
-  const uint64_t *hbase = reinterpret_cast<const uint64_t *>(h_out_ + q_base);
-  const uint32_t *hkey = reinterpret_cast<const uint32_t *>(h_out_ + q_key);
-  const uint32_t *htok = reinterpret_cast<const uint32_t *>(h_out_ + q_tok);
+  const uint32_t *hcount = reinterpret_cast<const uint32_t *>(h_out + q_count);
+  const double *hphase = reinterpret_cast<const double *>(h_out + q_phase);
+  const double *hlpn = reinterpret_cast<const double *>(h_out + q_lpn);
+  const uint32_t *hlen = reinterpret_cast<const uint32_t *>(h_out + q_len);
+  const uint64_t *hbase = reinterpret_cast<const uint64_t *>(h_out + q_base);
+  const uint32_t *hkey = reinterpret_cast<const uint32_t *>(h_out + q_key);
+  const uint32_t *htok = reinterpret_cast<const uint32_t *>(h_out + q_tok);
   for (uint32_t i = 0; i < n; ++i) {
     const uint32_t nb = hcount[i];
     ft_result &r = out[i];

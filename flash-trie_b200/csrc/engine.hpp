@@ -72,17 +72,14 @@ class Engine {
   std::vector<DevBuf> allocs_;
   // device workspace
   SlotView *d_slots_ = nullptr;
-  uint32_t *d_status_ = nullptr;      // host-buffer path: cleared per call
   uint32_t *d_status_dev_ = nullptr;  // device path: accumulates until read
   uint32_t *d_debug_ = nullptr;       // first failed kernel self-check
-  // staging: [meta | factor | beams | ids | logp] on device and pinned host
-  uint8_t *d_in_ = nullptr;
-  uint8_t *h_in_ = nullptr;
-  size_t in_bytes_ = 0;
-  // outputs: [status | count | phase | lpn | len | tok]
-  uint8_t *d_out_ = nullptr;
-  uint8_t *h_out_ = nullptr;
-  size_t out_bytes_ = 0;
+  // host-buffer path staging, on device and pinned host: a call's inputs
+  // [meta | factor | beams | ids | logp], then its outputs [status, token total |
+  // count | phase | lpn | len | key | token base | tok]
+  uint8_t *d_io_ = nullptr;
+  uint8_t *h_io_ = nullptr;
+  size_t in_bytes_ = 0, out_bytes_ = 0;
   // device-path meta/factor staging
   uint8_t *d_dmeta_ = nullptr;
   uint8_t *h_dmeta_ = nullptr;
