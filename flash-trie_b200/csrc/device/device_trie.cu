@@ -7,6 +7,7 @@
 
 #include "cuda_util.hpp"
 #include "device_trie.hpp"
+#include "tbs_kernel.cuh"
 
 namespace ftb {
 
@@ -233,6 +234,7 @@ void DeviceTrie::upload(const LoudsLevel &lv, int num_threads) {
     if (binary_tail) tail_end = upload_array(lv.tail_end_flags.units.data(), lv.tail_end_flags.units.size(), bytes);
     hash = upload_array(img.hash.data(), img.hash.size(), bytes);
     hash_slots = img.hash.size() / 2;
+    reserve_l2_persisting(device);
   } catch (...) {
     release();
     throw;

@@ -156,6 +156,11 @@ SearchLaunch plan_search(uint32_t n, size_t smem_bytes);
 
 // Enqueues the search kernel on `stream`: `grid` teams, one per in-flight
 // request (requests beyond `grid` are taken by teams that finish).
+// With FT_L2_PERSIST=1, sets aside the device's persisting L2 (once per
+// device and process) for the access-policy window every search launch then
+// puts on the upper levels of its trie; returns the bytes set aside (0: off).
+size_t reserve_l2_persisting(int device);
+
 void launch_search(const SearchParams &p, size_t smem_bytes, int grid, cudaStream_t stream, const SearchLaunch &l);
 
 // Teams of `cluster_size` CTAs that can be resident at once.
