@@ -37,6 +37,7 @@
 // sequence rebuilt from the history (tbs-kernels.cu:393-474), and with each
 // result's key id when asked.
 #include <algorithm>
+#include <cstddef>
 #include <map>
 #include <mutex>
 
@@ -217,6 +218,12 @@ struct alignas(16) LocalState {
   unsigned long long out_base;      // their first slot
   uint32_t stop;
 };
+// hist is read as uint4, super and part as uint2 (also over DSMEM).
+static_assert(offsetof(LocalState, hist) % 16 == 0 && (sizeof(uint32_t) * kRadixBins) % 16 == 0,
+              "LocalState::hist must stay 16-byte aligned");
+static_assert(offsetof(LocalState, super) % 8 == 0 && offsetof(LocalState, part) % 8 == 0 &&
+                  (sizeof(uint32_t) * kSuperBins) % 8 == 0,
+              "LocalState::super and part must stay 8-byte aligned");
 
 // Task table of a chunk of branching parents, in dynamic shared memory.
 struct BranchTable {
