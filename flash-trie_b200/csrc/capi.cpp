@@ -253,6 +253,16 @@ int ft_tbs_batch_device(ft_trie *trie, const ft_device_batch *batch, const ft_se
   });
 }
 
+int ft_lookup_batch_device(ft_trie *trie, uint32_t n, const uint32_t *tokens, const uint64_t *offsets,
+                           uint64_t total_tokens, uint32_t *out_ids, void *stream) {
+  return guarded([&] {
+    require_trie(trie);
+    if (!trie->engine)
+      ftb::fail(ftb::ErrorKind::kState, "MARISA_STATE_ERROR: init_tbs_gpu must be called before a GPU lookup");
+    trie->engine->lookup_device(n, tokens, offsets, total_tokens, out_ids, static_cast<cudaStream_t>(stream));
+  });
+}
+
 int ft_trie_device_status(ft_trie *trie, uint32_t *status) {
   return guarded([&] {
     require_trie(trie);

@@ -1506,6 +1506,104 @@ __global__ void __launch_bounds__(kSearchThreads, kMinBlocks) tbs_search_kernel(
   }
 }
 
+// ------------------------------------------------------------- lookup
+// Node reached from `node` by label x, or 0 (the root is nobody's child).
+__device__ __forceinline__ uint32_t find_child(const TrieView &t, uint32_t node, uint32_t x, uint32_t *status) {
+  const uint4 r = __ldg(t.node + node);
+  const uint32_t f = rec_flags(r.w), c0 = r.z;
+  uint32_t d = r.w & kFanoutMask;
+  if (d == kFanoutMask) {
+    const uint32_t end = (uint64_t)node + 1 < t.num_nodes ? __ldg(t.node + node + 1).z : (uint32_t)t.num_nodes;
+    d = end > c0 ? end - c0 : 0;
+  }
+  if (d == 0) return 0;
+  if ((uint64_t)c0 + d > t.num_nodes) {
+    atomicOr(status, kStatusNodeBounds);
+    return 0;
+  }
+  if (!(f & kNodeFlagLink) && (f & kNodeFlagHashed)) {
+    // The node's open-addressing table (load <= 1/2: an empty slot ends every probe).
+    const uint32_t lg = f >> 3, size = 1u << lg, mask = size - 1u;
+    if ((uint64_t)r.y + size > t.hash_slots) {
+      atomicOr(status, kStatusNodeBounds);
+      return 0;
+    }
+    uint32_t h = (x * 2654435761u) >> (32 - lg);
+    for (uint32_t probe = 0; probe < size; ++probe) {
+      const uint2 sl = __ldg(t.hash + r.y + h);
+      if (sl.y == 0) return 0;
+      if (sl.x == x) return sl.y < t.num_nodes ? sl.y : 0u;
+      h = (h + 1) & mask;
+    }
+    return 0;
+  }
+  // Child labels are sorted: binary search (the first word of each record).
+  const uint32_t *labs = reinterpret_cast<const uint32_t *>(t.node + c0);
+  uint32_t lo = 0, n = d;
+  while (n > 0) {
+    const uint32_t half = n >> 1;
+    if (__ldg(labs + 4ull * (lo + half)) < x) {
+      lo += half + 1;
+      n -= half + 1;
+    } else {
+      n = half;
+    }
+  }
+  return lo < d && __ldg(labs + 4ull * lo) == x ? c0 + lo : 0u;
+}
+
+// Key ids of n token sequences (reference LoudsTrie::lookup,
+// louds-trie.cc:56-72, with the find_child walk of :764-808): one thread per
+// key walks from the root; a link child matches its whole tail string.
+__global__ void __launch_bounds__(256) lookup_kernel(const TrieView t, const uint32_t *tokens,
+                                                     const uint64_t *offsets, uint32_t n, uint64_t total_tokens,
+                                                     uint32_t *out, uint32_t *status) {
+  for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < n; k += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t s = offsets[k], e = offsets[k + 1];
+    uint32_t id = 0xFFFFFFFFu;
+    if (s > e || e > total_tokens) {
+      atomicOr(status, kStatusBadRequest);
+      out[k] = id;
+      continue;
+    }
+    uint32_t node = 0;
+    bool found = t.num_nodes > 0;
+    for (uint64_t pos = s; found && pos < e;) {
+      const uint32_t child = find_child(t, node, tokens[pos], status);
+      if (child == 0) {
+        found = false;
+        break;
+      }
+      ++pos;
+      const uint4 cr = __ldg(t.node + child);
+      const uint32_t cf = rec_flags(cr.w);
+      if ((cf & kNodeFlagLink) && !(cf & kNodeFlagLinkEnds1)) {
+        // The rest of the link's string, after its first token (the label).
+        uint32_t off = cr.y + 1;
+        for (;;) {
+          bool ok;
+          const bool end = tail_ends_at(t, off, ok);
+          if (!ok) {
+            atomicOr(status, kStatusTailBounds);
+            found = false;
+            break;
+          }
+          if (pos >= e || __ldg(t.tail + off) != tokens[pos]) {
+            found = false;
+            break;
+          }
+          ++pos;
+          ++off;
+          if (end) break;
+        }
+      }
+      node = child;
+    }
+    if (found && (rec_flags(__ldg(t.node + node).w) & kNodeFlagTerminal)) id = key_id(t, node);
+    out[k] = id;
+  }
+}
+
 }  // namespace
 
 size_t search_smem_bytes(uint32_t max_topk, uint32_t max_final_beam) {
@@ -1671,6 +1769,14 @@ void launch_search(const SearchParams &p, size_t smem_bytes, int grid, cudaStrea
   } else {
     CUDA_TRY(cudaLaunchKernelEx(&cfg, tbs_search_kernel<1>, p));
   }
+}
+
+void launch_lookup(const TrieView &t, const uint32_t *tokens, const uint64_t *offsets, uint32_t n,
+                   uint64_t total_tokens, uint32_t *out, uint32_t *status, cudaStream_t stream) {
+  if (n == 0) return;
+  const uint32_t blocks = std::min<uint32_t>((n + 255) / 256, (uint32_t)sm_count() * 8u);
+  lookup_kernel<<<blocks, 256, 0, stream>>>(t, tokens, offsets, n, total_tokens, out, status);
+  CUDA_TRY(cudaGetLastError());
 }
 
 }  // namespace ftb

@@ -156,6 +156,12 @@ SearchLaunch plan_search(uint32_t n, size_t smem_bytes);
 
 // Enqueues the search kernel on `stream`: `grid` teams, one per in-flight
 // request (requests beyond `grid` are taken by teams that finish).
+// Key ids of n token sequences in device memory (key i is
+// tokens[offsets[i], offsets[i+1])) into out (0xFFFFFFFF: not a key), on
+// `stream`; bad offsets and trie inconsistencies set bits of *status.
+void launch_lookup(const TrieView &t, const uint32_t *tokens, const uint64_t *offsets, uint32_t n,
+                   uint64_t total_tokens, uint32_t *out, uint32_t *status, cudaStream_t stream);
+
 // With FT_L2_PERSIST=1, sets aside the device's persisting L2 (once per
 // device and process) for the access-policy window every search launch then
 // puts on the upper levels of its trie; returns the bytes set aside (0: off).

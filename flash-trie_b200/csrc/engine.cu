@@ -311,6 +311,16 @@ void Engine::search_device(const ft_device_batch &b, const ft_search_params &prm
   launch_search(sp, smem_, grid, stream, plan);
 }
 
+void Engine::lookup_device(uint32_t n, const uint32_t *tokens, const uint64_t *offsets, uint64_t total_tokens,
+                           uint32_t *out_ids, cudaStream_t stream) {
+  std::lock_guard<std::mutex> lock(mu_);
+  if (n == 0) return;
+  if (!tokens && total_tokens) throw InvalidArgument("lookup: tokens is NULL");
+  if (!offsets || !out_ids) throw InvalidArgument("lookup: offsets and out_ids must not be NULL");
+  CUDA_TRY(cudaSetDevice(device_));
+  launch_lookup(make_trie_view(*trie_), tokens, offsets, n, total_tokens, out_ids, d_status_dev_, stream);
+}
+
 uint32_t Engine::read_status() {
   std::lock_guard<std::mutex> lock(mu_);
   uint32_t s = 0;

@@ -52,6 +52,10 @@ class Engine {
   void search_host(const ft_request *reqs, uint32_t n, const ft_search_params &prm, ft_result *out);
   void search_device(const ft_device_batch &b, const ft_search_params &prm, cudaStream_t stream);
   uint32_t read_status();
+  // Key ids of n token sequences in device memory, on `stream` (bad offsets
+  // and trie inconsistencies go to the same status word as search_device).
+  void lookup_device(uint32_t n, const uint32_t *tokens, const uint64_t *offsets, uint64_t total_tokens,
+                     uint32_t *out_ids, cudaStream_t stream);
 
  private:
   struct DevBuf {

@@ -12,6 +12,7 @@ copy in between.  This is the C-ABI entry point `ft_tbs_batch_device`
     trie.init_tbs_gpu(64, max_num_topk=1000, max_num_outpos=20, max_num_out_beams=1000)
     out = fd.bs_tbs_device(trie, beams, topk_id, topk_logp, -10.0, -40.0, 5.0, False)
     sents, lpns = fd.to_lists(out)        # host lists, only when needed
+    ids = fd.lookup(trie, tokens, offsets)  # key ids of token sequences on the device
 
 Inputs (contiguous, on one CUDA device): beams int32 [n, L]; topk_id int32
 [n, L, K] (token ids, read as unsigned); topk_logp float32 [n, L, K].  Rows
@@ -49,6 +50,9 @@ def _lib():
         lib.ft_tbs_batch_device.argtypes = [ctypes.c_void_p, ctypes.POINTER(_Batch), ctypes.POINTER(_Params),
                                             ctypes.c_void_p]
         lib.ft_tbs_batch_device.restype = ctypes.c_int
+        lib.ft_lookup_batch_device.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p,
+                                               ctypes.c_uint64, ctypes.c_void_p, ctypes.c_void_p]
+        lib.ft_lookup_batch_device.restype = ctypes.c_int
         lib.ft_trie_device_status.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32)]
         lib.ft_trie_device_status.restype = ctypes.c_int
         lib.ft_last_error.restype = ctypes.c_char_p
@@ -123,6 +127,36 @@ def bs_tbs_device(trie, beams, topk_id, topk_logp, token_logp_threshold, sents_l
         st = device_status(trie)
         if st:
             raise RuntimeError("device search failed its self-checks or exceeded the workspace (status 0x%x)" % st)
+    return out
+
+
+def lookup(trie, tokens, offsets, stream=None, check=True):
+    """Key ids of n token sequences on the device: LoudsTrie::lookup for a
+    batch (C ABI ft_lookup_batch_device).  tokens: int32 CUDA tensor [T]
+    (ids read as unsigned); offsets: int64 CUDA tensor [n + 1], key i being
+    tokens[offsets[i]:offsets[i + 1]].  Returns an int32 tensor [n] of key
+    ids (the ids key_ids=True reports; read as unsigned), -1 where the
+    sequence is not a key.  check: synchronise and raise if the kernel
+    reported bad offsets or an inconsistent trie."""
+    _want(tokens, "tokens", torch.int32, 1, None)
+    dev = tokens.device
+    _want(offsets, "offsets", torch.int64, 1, dev)
+    n = offsets.numel() - 1
+    if n < 0:
+        raise ValueError("offsets must have n + 1 >= 1 entries")
+    out = torch.empty(n, dtype=torch.int32, device=dev)
+    if n == 0:
+        return out
+    if stream is None:
+        stream = torch.cuda.current_stream(dev)
+    with torch.cuda.device(dev):
+        _check(_lib().ft_lookup_batch_device(ctypes.c_void_p(trie.ft_handle()), n, ctypes.c_void_p(tokens.data_ptr()),
+                                             ctypes.c_void_p(offsets.data_ptr()), tokens.numel(),
+                                             ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(stream.cuda_stream)))
+    if check:
+        st = device_status(trie)
+        if st:
+            raise RuntimeError("device lookup reported bad offsets or an inconsistent trie (status 0x%x)" % st)
     return out
 
 

@@ -164,9 +164,22 @@ typedef struct {
 int ft_tbs_batch_device(ft_trie *trie, const ft_device_batch *batch,
                         const ft_search_params *params, void *stream);
 
-/* Status word of the device-resident searches since the last call (0 =
- * clean; the word is cleared by reading it); non-zero bits name the checks
- * that failed inside the kernel. */
+/*
+ * Replaces LoudsTrie::lookup (lib/marisa/grimoire/trie/louds-trie.cc:56-72)
+ * for a batch, on the device: key i is tokens[offsets[i] .. offsets[i+1]) and
+ * out_ids[i] receives its key id (the id ft_result.key_ids reports), or
+ * 0xFFFFFFFF when it is not a key of the trie.  tokens (total_tokens entries),
+ * offsets (n + 1 entries) and out_ids (n entries) are device pointers; the
+ * lookup runs on `stream` and the call returns without waiting.  Requires
+ * ft_trie_init_tbs_gpu.  Offsets that decrease or pass total_tokens give
+ * 0xFFFFFFFF for that key and set a bit of the device status word.
+ */
+int ft_lookup_batch_device(ft_trie *trie, uint32_t n, const uint32_t *tokens, const uint64_t *offsets,
+                           uint64_t total_tokens, uint32_t *out_ids, void *stream);
+
+/* Status word of the device-resident searches and lookups since the last call
+ * (0 = clean; the word is cleared by reading it); non-zero bits name the
+ * checks that failed inside the kernel. */
 int ft_trie_device_status(ft_trie *trie, uint32_t *status);
 
 /*

@@ -38,6 +38,11 @@ def test_host_entry_points_without_gpu(built, tmp_path):
     assert lib.ft_trie_save(h, p) == 0
     assert lib.ft_trie_load(h, b"/nonexistent/trie.bin") == -9  # FT_ERR_IO
     assert b"IO_ERROR" in lib.ft_last_error()
+    # A device lookup needs a GPU workspace: refused before any device call.
+    lib.ft_lookup_batch_device.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p,
+                                           ctypes.c_uint64, ctypes.c_void_p, ctypes.c_void_p]
+    assert lib.ft_lookup_batch_device(h, 1, None, None, 0, None, None) == -1  # FT_ERR_STATE
+    assert b"init_tbs_gpu" in lib.ft_last_error()
     lib.ft_trie_destroy(h)
 
 
@@ -54,3 +59,5 @@ def test_device_api_rejects_host_tensors(built):
     lp = torch.zeros((1, 2, 4), dtype=torch.float32)
     with pytest.raises(TypeError):
         fd.bs_tbs_device(t, beams, ids, lp, -10.0, -40.0, 1.0, False)
+    with pytest.raises(TypeError):
+        fd.lookup(t, torch.zeros(3, dtype=torch.int32), torch.zeros(2, dtype=torch.int64))
