@@ -263,6 +263,16 @@ int ft_lookup_batch_device(ft_trie *trie, uint32_t n, const uint32_t *tokens, co
   });
 }
 
+int ft_reverse_lookup_batch_device(ft_trie *trie, uint32_t n, const uint32_t *ids, uint32_t max_len,
+                                   uint32_t *out_tokens, uint32_t *out_len, void *stream) {
+  return guarded([&] {
+    require_trie(trie);
+    if (!trie->engine)
+      ftb::fail(ftb::ErrorKind::kState, "MARISA_STATE_ERROR: init_tbs_gpu must be called before a GPU lookup");
+    trie->engine->reverse_lookup_device(n, ids, max_len, out_tokens, out_len, static_cast<cudaStream_t>(stream));
+  });
+}
+
 int ft_trie_device_status(ft_trie *trie, uint32_t *status) {
   return guarded([&] {
     require_trie(trie);

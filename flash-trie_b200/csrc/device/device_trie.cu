@@ -183,6 +183,7 @@ void DeviceTrie::release() {
   tail_end = nullptr;
   hash = nullptr;
   hash_slots = 0;
+  num_keys = 0;
   device = -1;
   bytes = 0;
 }
@@ -228,6 +229,7 @@ void DeviceTrie::upload(const LoudsLevel &lv, int num_threads) {
         cum += (uint64_t)__builtin_popcountll(bits);
       }
       if (cum >= 0xFFFFFFFFull) fail(ErrorKind::kSize, "MARISA_SIZE_ERROR: too many keys for 32-bit key ids");
+      num_keys = cum;
       term_rank = upload_array(tr.data(), tr.size(), bytes);
     }
     tail = upload_array(lv.tail.data(), lv.tail.size(), bytes);

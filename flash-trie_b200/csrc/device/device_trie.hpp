@@ -78,6 +78,7 @@ struct DeviceTrie {
   uint64_t *tail_end = nullptr;
   uint32_t *hash = nullptr;
   uint64_t hash_slots = 0;
+  uint64_t num_keys = 0;  // terminal nodes
   uint64_t bytes = 0;
 
   DeviceTrie() = default;

@@ -1604,6 +1604,116 @@ __global__ void __launch_bounds__(256) lookup_kernel(const TrieView t, const uin
   }
 }
 
+// Parent of every node (LOUDS numbers children after their parent, so
+// parent[c] < c): each node writes itself into its children's entries.
+__global__ void __launch_bounds__(256) parents_kernel(const TrieView t, uint32_t *parent, uint32_t *status) {
+  for (uint64_t p = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; p < t.num_nodes;
+       p += (uint64_t)gridDim.x * blockDim.x) {
+    const uint4 r = __ldg(t.node + p);
+    const uint32_t c0 = r.z;
+    uint64_t d = r.w & kFanoutMask;
+    if (d == kFanoutMask) {
+      const uint64_t end = p + 1 < t.num_nodes ? (uint64_t)__ldg(t.node + p + 1).z : t.num_nodes;
+      d = end > c0 ? end - c0 : 0;
+    }
+    if (d == 0) continue;
+    if ((uint64_t)c0 + d > t.num_nodes || c0 <= p) {
+      atomicOr(status, kStatusNodeBounds);
+      continue;
+    }
+    for (uint64_t c = c0; c < (uint64_t)c0 + d; ++c) parent[c] = (uint32_t)p;
+  }
+}
+
+// Tokens a node contributes to its keys: its label, or a link node's whole
+// tail string (which starts with the label).  Returns the count (0 and a
+// status bit on a tail inconsistency); writes them to `out` when non-null.
+__device__ __forceinline__ uint32_t node_tokens(const TrieView &t, uint32_t m, uint32_t *out, uint32_t *status) {
+  const uint4 r = __ldg(t.node + m);
+  if (!(rec_flags(r.w) & kNodeFlagLink)) {
+    if (out) out[0] = r.x;
+    return 1;
+  }
+  uint32_t n = 0;
+  for (uint32_t off = r.y;; ++off) {
+    bool ok;
+    const bool end = tail_ends_at(t, off, ok);
+    if (!ok) {
+      atomicOr(status, kStatusTailBounds);
+      return 0;
+    }
+    if (out) out[n] = __ldg(t.tail + off);
+    ++n;
+    if (end) return n;
+  }
+}
+
+// Token sequences of key ids (reference LoudsTrie::reverse_lookup,
+// louds-trie.cc:179-210): the id-th terminal node is found in the
+// terminal-rank directory, then the walk to the root collects each node's
+// tokens, back to front.  out_len[k] = the key's length (0xFFFFFFFF: not a
+// key id); its tokens are written when they fit in max_len.
+__global__ void __launch_bounds__(256) reverse_lookup_kernel(const TrieView t, const uint32_t *parent,
+                                                             uint64_t num_keys, const uint32_t *ids, uint32_t n,
+                                                             uint32_t max_len, uint32_t *out_tok, uint32_t *out_len,
+                                                             uint32_t *status) {
+  const uint64_t blocks = (t.num_nodes + 63) / 64;
+  for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < n; k += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t id = ids[k];
+    if ((uint64_t)id >= num_keys || blocks == 0) {
+      out_len[k] = 0xFFFFFFFFu;
+      continue;
+    }
+    // Last block whose count of earlier terminals is <= id holds the id-th.
+    uint64_t lo = 0, cnt = blocks;
+    while (cnt > 1) {
+      const uint64_t half = cnt >> 1;
+      if (__ldg(t.term_rank + lo + half).x <= id) {
+        lo += half;
+        cnt -= half;
+      } else {
+        cnt = half;
+      }
+    }
+    const uint4 b = __ldg(t.term_rank + lo);
+    uint64_t bits = ((uint64_t)b.w << 32) | b.z;
+    for (uint32_t r = id - b.x; r > 0 && bits; --r) bits &= bits - 1;
+    if (!bits || b.x > id) {
+      atomicOr(status, kStatusNodeBounds);
+      out_len[k] = 0xFFFFFFFFu;
+      continue;
+    }
+    const uint32_t node = (uint32_t)(lo * 64 + (uint64_t)(__ffsll((long long)bits) - 1));
+    // Length, then the tokens back to front.
+    uint64_t len = 0;
+    bool ok = true;
+    for (uint32_t m = node; m != 0;) {
+      const uint32_t c = node_tokens(t, m, nullptr, status);
+      const uint32_t up = parent[m];
+      if (c == 0 || up >= m) {
+        ok = false;
+        break;
+      }
+      len += c;
+      m = up;
+    }
+    if (!ok || len > 0xFFFFFFFEull) {
+      atomicOr(status, kStatusNodeBounds);
+      out_len[k] = 0xFFFFFFFFu;
+      continue;
+    }
+    out_len[k] = (uint32_t)len;
+    if (len > max_len) continue;
+    uint32_t *dst = out_tok + k * (uint64_t)max_len;
+    uint64_t pos = len;
+    for (uint32_t m = node; m != 0; m = parent[m]) {
+      const uint32_t c = node_tokens(t, m, nullptr, status);
+      pos -= c;
+      node_tokens(t, m, dst + pos, status);
+    }
+  }
+}
+
 }  // namespace
 
 size_t search_smem_bytes(uint32_t max_topk, uint32_t max_final_beam) {
@@ -1776,6 +1886,23 @@ void launch_lookup(const TrieView &t, const uint32_t *tokens, const uint64_t *of
   if (n == 0) return;
   const uint32_t blocks = std::min<uint32_t>((n + 255) / 256, (uint32_t)sm_count() * 8u);
   lookup_kernel<<<blocks, 256, 0, stream>>>(t, tokens, offsets, n, total_tokens, out, status);
+  CUDA_TRY(cudaGetLastError());
+}
+
+void launch_parents(const TrieView &t, uint32_t *parent, uint32_t *status, cudaStream_t stream) {
+  if (t.num_nodes == 0) return;
+  const uint64_t want = (t.num_nodes + 255) / 256;
+  const uint32_t blocks = (uint32_t)std::min<uint64_t>(want, (uint64_t)sm_count() * 8u);
+  parents_kernel<<<blocks, 256, 0, stream>>>(t, parent, status);
+  CUDA_TRY(cudaGetLastError());
+}
+
+void launch_reverse_lookup(const TrieView &t, const uint32_t *parent, uint64_t num_keys, const uint32_t *ids,
+                           uint32_t n, uint32_t max_len, uint32_t *out_tok, uint32_t *out_len, uint32_t *status,
+                           cudaStream_t stream) {
+  if (n == 0) return;
+  const uint32_t blocks = std::min<uint32_t>((n + 255) / 256, (uint32_t)sm_count() * 8u);
+  reverse_lookup_kernel<<<blocks, 256, 0, stream>>>(t, parent, num_keys, ids, n, max_len, out_tok, out_len, status);
   CUDA_TRY(cudaGetLastError());
 }
 

@@ -162,6 +162,16 @@ SearchLaunch plan_search(uint32_t n, size_t smem_bytes);
 void launch_lookup(const TrieView &t, const uint32_t *tokens, const uint64_t *offsets, uint32_t n,
                    uint64_t total_tokens, uint32_t *out, uint32_t *status, cudaStream_t stream);
 
+// parent[c] for every node c (parent[0] = 0), on `stream`.
+void launch_parents(const TrieView &t, uint32_t *parent, uint32_t *status, cudaStream_t stream);
+
+// Token sequences of n key ids (see reverse_lookup_kernel), on `stream`:
+// out_len[k] = length of key ids[k] (0xFFFFFFFF: not a key id); its tokens go
+// to out_tok[k * max_len ...] when the length is at most max_len.
+void launch_reverse_lookup(const TrieView &t, const uint32_t *parent, uint64_t num_keys, const uint32_t *ids,
+                           uint32_t n, uint32_t max_len, uint32_t *out_tok, uint32_t *out_len, uint32_t *status,
+                           cudaStream_t stream);
+
 // With FT_L2_PERSIST=1, sets aside the device's persisting L2 (once per
 // device and process) for the access-policy window every search launch then
 // puts on the upper levels of its trie; returns the bytes set aside (0: off).

@@ -321,6 +321,24 @@ void Engine::lookup_device(uint32_t n, const uint32_t *tokens, const uint64_t *o
   launch_lookup(make_trie_view(*trie_), tokens, offsets, n, total_tokens, out_ids, d_status_dev_, stream);
 }
 
+void Engine::reverse_lookup_device(uint32_t n, const uint32_t *ids, uint32_t max_len, uint32_t *out_tokens,
+                                   uint32_t *out_len, cudaStream_t stream) {
+  std::lock_guard<std::mutex> lock(mu_);
+  if (n == 0) return;
+  if (!ids || !out_len || (max_len && !out_tokens))
+    throw InvalidArgument("reverse_lookup: ids, out_len and out_tokens must not be NULL");
+  CUDA_TRY(cudaSetDevice(device_));
+  const TrieView tv = make_trie_view(*trie_);
+  if (!d_parent_) {
+    uint32_t *p = (uint32_t *)dalloc(sizeof(uint32_t) * std::max<uint64_t>(trie_->num_nodes, 1));
+    CUDA_TRY(cudaMemsetAsync(p, 0, sizeof(uint32_t) * std::max<uint64_t>(trie_->num_nodes, 1), stream_));
+    launch_parents(tv, p, d_status_dev_, stream_);
+    CUDA_TRY(cudaStreamSynchronize(stream_));
+    d_parent_ = p;
+  }
+  launch_reverse_lookup(tv, d_parent_, trie_->num_keys, ids, n, max_len, out_tokens, out_len, d_status_dev_, stream);
+}
+
 uint32_t Engine::read_status() {
   std::lock_guard<std::mutex> lock(mu_);
   uint32_t s = 0;

@@ -56,6 +56,10 @@ class Engine {
   // and trie inconsistencies go to the same status word as search_device).
   void lookup_device(uint32_t n, const uint32_t *tokens, const uint64_t *offsets, uint64_t total_tokens,
                      uint32_t *out_ids, cudaStream_t stream);
+  // Token sequences of n key ids in device memory, on `stream`; the first
+  // call derives the nodes' parents (4 bytes per node, kept with the workspace).
+  void reverse_lookup_device(uint32_t n, const uint32_t *ids, uint32_t max_len, uint32_t *out_tokens,
+                             uint32_t *out_len, cudaStream_t stream);
 
  private:
   struct DevBuf {
@@ -78,6 +82,7 @@ class Engine {
   SlotView *d_slots_ = nullptr;
   uint32_t *d_status_dev_ = nullptr;  // device path: accumulates until read
   uint32_t *d_debug_ = nullptr;       // first failed kernel self-check
+  uint32_t *d_parent_ = nullptr;      // parent of every node, derived at the first reverse lookup
   // host-buffer path staging, on device and pinned host: a call's inputs
   // [meta | factor | beams | ids | logp], then its outputs [status, token total |
   // count | phase | lpn | len | key | token base | tok]

@@ -13,6 +13,7 @@ copy in between.  This is the C-ABI entry point `ft_tbs_batch_device`
     out = fd.bs_tbs_device(trie, beams, topk_id, topk_logp, -10.0, -40.0, 5.0, False)
     sents, lpns = fd.to_lists(out)        # host lists, only when needed
     ids = fd.lookup(trie, tokens, offsets)  # key ids of token sequences on the device
+    toks, lens = fd.reverse_lookup(trie, ids, max_len=20)  # and back
 
 Inputs (contiguous, on one CUDA device): beams int32 [n, L]; topk_id int32
 [n, L, K] (token ids, read as unsigned); topk_logp float32 [n, L, K].  Rows
@@ -53,6 +54,10 @@ def _lib():
         lib.ft_lookup_batch_device.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p,
                                                ctypes.c_uint64, ctypes.c_void_p, ctypes.c_void_p]
         lib.ft_lookup_batch_device.restype = ctypes.c_int
+        lib.ft_reverse_lookup_batch_device.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p,
+                                                       ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p,
+                                                       ctypes.c_void_p]
+        lib.ft_reverse_lookup_batch_device.restype = ctypes.c_int
         lib.ft_trie_device_status.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32)]
         lib.ft_trie_device_status.restype = ctypes.c_int
         lib.ft_last_error.restype = ctypes.c_char_p
@@ -158,6 +163,38 @@ def lookup(trie, tokens, offsets, stream=None, check=True):
         if st:
             raise RuntimeError("device lookup reported bad offsets or an inconsistent trie (status 0x%x)" % st)
     return out
+
+
+def reverse_lookup(trie, ids, max_len, stream=None, check=True):
+    """Token sequences of key ids on the device: LoudsTrie::reverse_lookup
+    for a batch (C ABI ft_reverse_lookup_batch_device).  ids: int32 CUDA
+    tensor [n] (read as unsigned).  Returns (tokens int32 [n, max_len],
+    lengths int32 [n]): key i is tokens[i, :lengths[i]] when lengths[i] <=
+    max_len (longer keys report their length and write no tokens); -1 marks
+    an id that is not a key id.  The first call derives the trie's parent
+    links on the device once."""
+    _want(ids, "ids", torch.int32, 1, None)
+    dev = ids.device
+    n = ids.numel()
+    max_len = int(max_len)
+    if max_len < 0:
+        raise ValueError("max_len must be >= 0")
+    toks = torch.zeros((n, max(max_len, 1)), dtype=torch.int32, device=dev)
+    lens = torch.empty(n, dtype=torch.int32, device=dev)
+    if n == 0:
+        return toks[:, :max_len], lens
+    if stream is None:
+        stream = torch.cuda.current_stream(dev)
+    with torch.cuda.device(dev):
+        _check(_lib().ft_reverse_lookup_batch_device(ctypes.c_void_p(trie.ft_handle()), n,
+                                                     ctypes.c_void_p(ids.data_ptr()), max_len,
+                                                     ctypes.c_void_p(toks.data_ptr()), ctypes.c_void_p(lens.data_ptr()),
+                                                     ctypes.c_void_p(stream.cuda_stream)))
+    if check:
+        st = device_status(trie)
+        if st:
+            raise RuntimeError("device reverse lookup found an inconsistent trie (status 0x%x)" % st)
+    return toks[:, :max_len], lens
 
 
 def to_lists(out):

@@ -177,6 +177,19 @@ int ft_tbs_batch_device(ft_trie *trie, const ft_device_batch *batch,
 int ft_lookup_batch_device(ft_trie *trie, uint32_t n, const uint32_t *tokens, const uint64_t *offsets,
                            uint64_t total_tokens, uint32_t *out_ids, void *stream);
 
+/*
+ * Replaces LoudsTrie::reverse_lookup (lib/marisa/grimoire/trie/louds-trie.cc:179-210)
+ * for a batch, on the device: out_len[i] receives the length of the key whose
+ * id is ids[i] (0xFFFFFFFF when ids[i] is not a key id), and its tokens go to
+ * out_tokens[i * max_len ...] when that length is at most max_len.  ids (n),
+ * out_tokens (n * max_len) and out_len (n) are device pointers; the lookup
+ * runs on `stream` and the call returns without waiting.  Requires
+ * ft_trie_init_tbs_gpu; the first call derives every node's parent (4 bytes
+ * per node, freed with the workspace) and waits for that once.
+ */
+int ft_reverse_lookup_batch_device(ft_trie *trie, uint32_t n, const uint32_t *ids, uint32_t max_len,
+                                   uint32_t *out_tokens, uint32_t *out_len, void *stream);
+
 /* Status word of the device-resident searches and lookups since the last call
  * (0 = clean; the word is cleared by reading it); non-zero bits name the
  * checks that failed inside the kernel. */

@@ -43,6 +43,10 @@ def test_host_entry_points_without_gpu(built, tmp_path):
                                            ctypes.c_uint64, ctypes.c_void_p, ctypes.c_void_p]
     assert lib.ft_lookup_batch_device(h, 1, None, None, 0, None, None) == -1  # FT_ERR_STATE
     assert b"init_tbs_gpu" in lib.ft_last_error()
+    lib.ft_reverse_lookup_batch_device.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p,
+                                                   ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p,
+                                                   ctypes.c_void_p]
+    assert lib.ft_reverse_lookup_batch_device(h, 1, None, 4, None, None, None) == -1  # FT_ERR_STATE
     lib.ft_trie_destroy(h)
 
 
@@ -61,3 +65,5 @@ def test_device_api_rejects_host_tensors(built):
         fd.bs_tbs_device(t, beams, ids, lp, -10.0, -40.0, 1.0, False)
     with pytest.raises(TypeError):
         fd.lookup(t, torch.zeros(3, dtype=torch.int32), torch.zeros(2, dtype=torch.int64))
+    with pytest.raises(TypeError):
+        fd.reverse_lookup(t, torch.zeros(3, dtype=torch.int32), 4)

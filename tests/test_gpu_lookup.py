@@ -2,7 +2,10 @@
 token sequences, compared with the oracle's lookup_id (itself pinned against
 the reference's own lookup tool) on keys, their prefixes and extensions,
 perturbed keys and random sequences, over tries with hashed nodes, link
-nodes, text and binary tails."""
+nodes, text and binary tails.  Device reverse lookup
+(ft_reverse_lookup_batch_device / flashtrie_device.reverse_lookup): every key
+id of a trie gives back exactly the trie's keys, each one the key the
+oracle's lookup_id maps to that id."""
 import numpy as np
 import pytest
 
@@ -122,3 +125,48 @@ def test_lookup_rejects_bad_offsets(built, tmp_path):
     assert ok[0] != -1 and ok[1] != -1 and ok[2] == -1  # [1,2], [3], [] (not a key)
     with pytest.raises(TypeError):
         fd.lookup(t, tok.cpu(), torch.tensor([0, 1], dtype=torch.int64, device="cuda"))
+
+
+def _check_reverse(trie, path, keys, max_len):
+    import torch
+    import flashtrie_device as fd
+    from oracle.oracle import OracleTrie
+    o = OracleTrie(path)
+    n_keys = o.num_keys()
+    ids = np.arange(n_keys + 2, dtype=np.uint32)
+    ids[-1] = 0xFFFFFFFF  # not key ids: n_keys and 2^32 - 1
+    toks, lens = fd.reverse_lookup(trie, torch.from_numpy(ids.view(np.int32)).cuda(), max_len)
+    toks, lens = toks.cpu().numpy().view(np.uint32), lens.cpu().numpy()
+    assert lens[-1] == -1 and lens[-2] == -1
+    got = []
+    for i in range(n_keys):
+        assert 0 <= lens[i], i
+        if lens[i] > max_len:
+            continue
+        seq = toks[i, :lens[i]].tolist()
+        assert o.lookup_id(seq) == i, (i, seq)
+        got.append(tuple(seq))
+    want = {tuple(k) for k in keys if len(k) <= max_len}
+    assert set(got) == want and len(got) == len(want)
+    assert int((lens[:n_keys] > max_len).sum()) == len({tuple(k) for k in keys if len(k) > max_len})
+
+
+def test_reverse_lookup_returns_every_key(built, tmp_path):
+    cfg = dict(W.CONFIGS[1])
+    tok, off = W.gen_keys(30000, cfg["vocab"], cfg["len_lo"], cfg["len_hi"], cfg["zipf"], seed=57)
+    keys = W.key_rows(tok, off)
+    t, p = _trie(tmp_path, keys, "rc1")
+    _check_reverse(t, p, keys, 8)
+    _check_reverse(t, p, keys, 5)  # longer keys report their length only
+    g = load_json("search_hand.json")
+    for name, ks in g["keysets"].items():
+        t, p = _trie(tmp_path, ks, "rh_" + name)
+        _check_reverse(t, p, ks, 16)
+    special = [[0xFFFFFFFF, 3, 4], [1, 2, 3], [1, 2, 4], [], [5] * 9]
+    t, p = _trie(tmp_path, special, "rspecial")
+    _check_reverse(t, p, special, 12)
+    rng = np.random.default_rng(61)
+    for vocab in (3, 5000):
+        ks = [rng.integers(0, vocab, size=int(rng.integers(1, 14))).tolist() for _ in range(4000)]
+        t, p = _trie(tmp_path, ks, "rr%d" % vocab)
+        _check_reverse(t, p, ks, 14)
