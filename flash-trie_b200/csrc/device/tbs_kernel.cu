@@ -36,15 +36,18 @@
 // After the last step the pool is sorted and written ascending with each
 // sequence rebuilt from the history (tbs-kernels.cu:393-474), and with each
 // result's key id when asked.
+//
+// The same file holds the batched key lookups over the same device image:
+// lookup_kernel (token sequence -> key id) and reverse_lookup_kernel (key id
+// -> token sequence, over parents derived by parents_kernel).
 #include <algorithm>
 #include <cstddef>
+#include <cstdlib>
 #include <map>
 #include <mutex>
 
 #include <cooperative_groups.h>
 #include <cooperative_groups/reduce.h>
-
-#include <cstdlib>
 
 #include "cuda_util.hpp"
 #include "tbs_kernel.cuh"
