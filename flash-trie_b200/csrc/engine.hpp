@@ -93,6 +93,9 @@ class Engine {
   uint8_t *d_dmeta_ = nullptr;
   uint8_t *h_dmeta_ = nullptr;
   size_t dmeta_bytes_ = 0;
+  // shape and length norm of what d_dmeta_ holds (n = 0: nothing yet)
+  uint32_t dmeta_L_ = 0, dmeta_K_ = 0, dmeta_n_ = 0;
+  double dmeta_ln_ = 0.0;
   cudaStream_t stream_ = nullptr;
   cudaEvent_t dmeta_done_ = nullptr;
   std::mutex mu_;

@@ -91,3 +91,26 @@ def test_beam_width_above_1024_matches_oracle(built, tmp_path):
             o_s, o_l = o.tbs(beams[i], ids[i], lp[i], thr[0], thr[1], 5.0, False)
             assert same_result(sents[i], lpns[i], o_s, o_l), (i, thr)
         assert max(len(s) for s in sents) > 1024  # results wider than 1024 beams
+
+
+def test_device_calls_with_changing_shape_and_length_norm(built, tmp_path):
+    """The device path reuses its uploaded meta and factor tables while the
+    batch shape and length norm stay the same: every change must show."""
+    import torch
+    import flashtrie
+    import flashtrie_device as fd
+    p, tok, off, cfg = _trie(tmp_path, n_keys=20000, seed=27)
+    beams, ids, lp = W.gen_requests(1, tok, off, 10, cfg=cfg)
+    t = flashtrie.Trie()
+    t.load(p)
+    t.init_tbs_gpu(10, max_num_topk=cfg["K"], max_num_outpos=cfg["L"], max_num_out_beams=cfg["beam"])
+    dev = torch.device("cuda:0")
+    for n, L, ln in [(10, 8, 5.0), (10, 8, 5.0), (10, 8, 1.0), (4, 8, 1.0), (10, 8, 1.0), (6, 5, 1.0), (6, 5, 0.0)]:
+        b, i_, l_ = beams[:n, :L].copy(), ids[:n, :L].copy(), lp[:n, :L].copy()
+        out = fd.bs_tbs_device(t, torch.from_numpy(b.astype(np.int32)).to(dev),
+                               torch.from_numpy(i_.view(np.int32)).to(dev), torch.from_numpy(l_).to(dev),
+                               -10.0, -40.0, ln, False)
+        d_sents, d_lpns = fd.to_lists(out)
+        h_sents, h_lpns, _, _ = flashtrie.bs_tbs_gpu(t, n, b, i_, l_, -10.0, -40.0, ln, False)
+        for r in range(n):
+            assert same_result(d_sents[r], d_lpns[r], h_sents[r], h_lpns[r]), (n, L, ln, r)
