@@ -32,8 +32,14 @@ typedef struct oracle_trie oracle_trie;
 
 #define ORACLE_MAX_STEPS 256
 
-/* Per-request counters; `bytes_alg` follows the algorithmic byte model the
- * engine's roofline uses (see DESIGN.md "algorithmic bytes"). */
+/* Per-request counters; `bytes_alg` is the algorithmic byte count the
+ * engine's roofline divides by its time: K*8 per step (the row); 32 per
+ * in-link parent (its tail cells) and 32 more when its link ends (terminal
+ * flag); 32 per branching parent (child range) plus
+ * 32*min(ceil(d/8)+1, K*ceil(log2(d+1))) for its child labels; 32 per matched
+ * child (flags) and 64 more per matched link child (link offset, next tail
+ * cells); 64 per candidate or pool entry (written, then read at selection);
+ * 12 + 4*len per output beam. */
 typedef struct {
   uint32_t steps_run;
   uint64_t parents_inlink[ORACLE_MAX_STEPS];
