@@ -23,10 +23,14 @@ Fixtures (JSON):
                 key ids the reference's own lookup tool (tools/marisa-lookup.cc,
                 built by oracle/ref.mk) reports on the config-1 trie for keys,
                 prefixes of keys and random sequences (-1: not a key).
+  topk_loader.json
+                a seeded top-k dataset directory (its two text files) and what
+                the reference's `load_topk_keys_and_scores` returns for it.
 The reference never runs on the GPU box; only these files travel.
 
     python tests/golden/make_golden.py           # all fixtures
     python tests/golden/make_golden.py lookup    # lookup_c1.json only
+    python tests/golden/make_golden.py topk      # topk_loader.json only
 """
 import hashlib
 import json
@@ -104,6 +108,50 @@ def lookup_golden(tok, off, path):
     assert len(ids) == len(queries)
     with open(os.path.join(HERE, "lookup_c1.json"), "w") as f:
         json.dump({"trie_sha256": file_sha(path), "queries": queries, "ids": ids}, f)
+
+
+def topk_loader_texts():
+    """The two text files of a seeded top-k dataset directory in the layout the
+    reference loader reads (tools/beam-search-helper.h:28-126): a header line
+    `num_requests max_output_len topk` in each file, then one line per
+    (request, depth) of ids / log-probabilities.  Rows cover the cases the
+    loader treats differently: depth 0 (kept in file order), deeper rows out
+    of id order (sorted by id, scores permuted with them), duplicate ids,
+    rows shorter than topk (padded with UINT32_MAX / -FLT_MAX), rows longer
+    than topk (truncated after sorting), ids written as floats ("12.0",
+    "12e0"), and an empty row."""
+    rng = np.random.default_rng(23)
+    n_req, max_len, topk = 4, 5, 6
+    k_lines = ["%d %d %d" % (n_req, max_len, topk)]
+    s_lines = ["%d %d %d" % (n_req, max_len, topk)]
+    for r in range(n_req):
+        for d in range(max_len):
+            width = [topk, topk - 2, topk + 3, 0, topk][(r + d) % 5]
+            ids = rng.integers(0, 400, size=width).tolist()
+            if width > 2 and d % 2 == 1:
+                ids[1] = ids[0]  # a duplicate id in the row
+            lp = np.sort(rng.normal(-3.0, 2.0, size=width).astype(np.float32))[::-1]
+            words = []
+            for j, x in enumerate(ids):
+                words.append("%d.0" % x if j % 4 == 1 else "%de0" % x if j % 4 == 3 else str(x))
+            k_lines.append(" ".join(words))
+            s_lines.append(" ".join(repr(float(v)) for v in lp))
+    return "\n".join(k_lines) + "\n", "\n".join(s_lines) + "\n"
+
+
+def topk_loader_golden():
+    import tempfile
+    import flashtrie_ref as ref
+    keys_txt, scores_txt = topk_loader_texts()
+    with tempfile.TemporaryDirectory() as d:
+        with open(os.path.join(d, "topk_keys.txt"), "w") as f:
+            f.write(keys_txt)
+        with open(os.path.join(d, "topk_scores.txt"), "w") as f:
+            f.write(scores_txt)
+        keys, scores = ref.load_topk_keys_and_scores(d)
+    with open(os.path.join(HERE, "topk_loader.json"), "w") as f:
+        json.dump({"topk_keys_txt": keys_txt, "topk_scores_txt": scores_txt, "ref_keys": keys,
+                   "ref_scores": scores}, f)
 
 
 def main():
@@ -192,7 +240,10 @@ if __name__ == "__main__":
     if sys.argv[1:] == ["lookup"]:
         _, tok, off, path = c1_reference_trie()
         lookup_golden(tok, off, path)
+    elif sys.argv[1:] == ["topk"]:
+        topk_loader_golden()
     else:
         main()
         _, tok, off, path = c1_reference_trie()
         lookup_golden(tok, off, path)
+        topk_loader_golden()
