@@ -26,11 +26,15 @@ Fixtures (JSON):
   topk_loader.json
                 a seeded top-k dataset directory (its two text files) and what
                 the reference's `load_topk_keys_and_scores` returns for it.
+  api_surface.json
+                the signature line of every public function and Trie method
+                of the reference module (names, keyword names, defaults).
 The reference never runs on the GPU box; only these files travel.
 
     python tests/golden/make_golden.py           # all fixtures
     python tests/golden/make_golden.py lookup    # lookup_c1.json only
     python tests/golden/make_golden.py topk      # topk_loader.json only
+    python tests/golden/make_golden.py api       # api_surface.json only
 """
 import hashlib
 import json
@@ -154,6 +158,20 @@ def topk_loader_golden():
                    "ref_scores": scores}, f)
 
 
+def api_golden():
+    """The first (signature) line of every public function and Trie method's
+    docstring in the reference module, as pybind11 writes it."""
+    import flashtrie_ref as ref
+
+    def sig(obj):
+        return (obj.__doc__ or "").strip().split("\n")[0]
+
+    surface = {"functions": {n: sig(getattr(ref, n)) for n in dir(ref) if not n.startswith("_") and n != "Trie"},
+               "Trie": {n: sig(getattr(ref.Trie, n)) for n in dir(ref.Trie) if not n.startswith("_")}}
+    with open(os.path.join(HERE, "api_surface.json"), "w") as f:
+        json.dump(surface, f, indent=1)
+
+
 def main():
     import flashtrie_ref as ref
     from oracle.oracle import OracleTrie
@@ -242,8 +260,11 @@ if __name__ == "__main__":
         lookup_golden(tok, off, path)
     elif sys.argv[1:] == ["topk"]:
         topk_loader_golden()
+    elif sys.argv[1:] == ["api"]:
+        api_golden()
     else:
         main()
         _, tok, off, path = c1_reference_trie()
         lookup_golden(tok, off, path)
         topk_loader_golden()
+        api_golden()
