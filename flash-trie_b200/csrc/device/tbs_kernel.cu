@@ -45,6 +45,8 @@
 #include <cstdlib>
 #include <map>
 #include <mutex>
+#include <tuple>
+#include <utility>
 
 #include <cooperative_groups.h>
 #include <cooperative_groups/reduce.h>
@@ -1746,10 +1748,39 @@ static int raise_smem(size_t search_smem) {
   return per_sm;
 }
 
+// Launch-planning answers of the driver, per device: the SM count, and how
+// many teams (or, for the two-CTAs-per-SM instance, CTAs per SM) fit for a
+// team size and dynamic shared-memory size.  They do not change while the
+// process runs, and asking the driver again on every search call would add
+// its cost to every synchronous search.  Callers raise the kernels'
+// shared-memory limit (ensure_search_smem) before planning a launch with
+// that size, so a remembered answer is never one taken under a lower limit.
+namespace {
+struct PlanCache {
+  std::mutex mu;
+  std::map<int, int> sms;                                   // device -> SMs
+  std::map<std::tuple<int, int, size_t>, int> clusters;     // (device, team size, smem) -> teams
+  std::map<std::pair<int, size_t>, int> dense_per_sm;       // (device, smem) -> CTAs per SM
+};
+PlanCache &plan_cache() {
+  static PlanCache c;
+  return c;
+}
+}  // namespace
+
 static int sm_count() {
-  int dev = 0, sms = 0;
+  int dev = 0;
   CUDA_TRY(cudaGetDevice(&dev));
+  PlanCache &pc = plan_cache();
+  {
+    std::lock_guard<std::mutex> lock(pc.mu);
+    auto it = pc.sms.find(dev);
+    if (it != pc.sms.end()) return it->second;
+  }
+  int sms = 0;
   CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  std::lock_guard<std::mutex> lock(pc.mu);
+  pc.sms[dev] = sms;
   return sms;
 }
 
@@ -1759,6 +1790,15 @@ int ensure_search_smem(size_t search_smem) {
 }
 
 int max_search_clusters(int cluster_size, size_t smem_bytes) {
+  int dev = 0;
+  CUDA_TRY(cudaGetDevice(&dev));
+  PlanCache &pc = plan_cache();
+  const auto key = std::make_tuple(dev, cluster_size, smem_bytes);
+  {
+    std::lock_guard<std::mutex> lock(pc.mu);
+    auto it = pc.clusters.find(key);
+    if (it != pc.clusters.end()) return it->second;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(cluster_size, 1, 1);
   cfg.blockDim = dim3(kSearchThreads, 1, 1);
@@ -1772,6 +1812,8 @@ int max_search_clusters(int cluster_size, size_t smem_bytes) {
   cfg.numAttrs = 1;
   int n = 0;
   CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, (void *)tbs_search_kernel<1>, &cfg));
+  std::lock_guard<std::mutex> lock(pc.mu);
+  pc.clusters[key] = n;
   return n;
 }
 
@@ -1798,8 +1840,21 @@ SearchLaunch plan_search(uint32_t n, size_t smem_bytes) {
   bool dense_ok = l.cluster_size == 1 && n > (uint32_t)sms;
   if (const char *e = getenv("FT_DENSE")) dense_ok = l.cluster_size == 1 && atoi(e) != 0;
   if (dense_ok) {
-    int per_sm = 0;
-    CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tbs_search_kernel<2>, kSearchThreads, smem_bytes));
+    int dev = 0;
+    CUDA_TRY(cudaGetDevice(&dev));
+    PlanCache &pc = plan_cache();
+    int per_sm = -1;
+    {
+      std::lock_guard<std::mutex> lock(pc.mu);
+      auto it = pc.dense_per_sm.find({dev, smem_bytes});
+      if (it != pc.dense_per_sm.end()) per_sm = it->second;
+    }
+    if (per_sm < 0) {
+      CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tbs_search_kernel<2>, kSearchThreads,
+                                                             smem_bytes));
+      std::lock_guard<std::mutex> lock(pc.mu);
+      pc.dense_per_sm[{dev, smem_bytes}] = per_sm;
+    }
     if (per_sm >= 2) {
       l.dense = 1;
       l.max_teams = per_sm * sms;
