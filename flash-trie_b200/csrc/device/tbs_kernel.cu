@@ -29,8 +29,10 @@
 //        to the result pool (one warp-wide reservation per task);
 //   3. select: exact top-beams[t] of the candidates in the pinned order
 //      (logp_norm, node, depth, score), an 11-bit MSD radix select over the
-//      192-bit key starting after the bits all candidates share; survivors
-//      become the next step's beams and append (parent, token) history;
+//      192-bit key starting after the bits all candidates share (its first
+//      pass bins logp_norm linearly when the values span a wide range);
+//      survivors become the next step's beams and append (parent, token)
+//      history;
 //   4. trim the result pool to the final beam the same way when the next
 //      step could overflow it.
 // After the last step the pool is sorted and written ascending with each
@@ -222,6 +224,15 @@ struct alignas(16) LocalState {
   uint32_t out_total;               // tokens of the request's result (compact output)
   unsigned long long out_base;      // their first slot
   uint32_t stop;
+  // Value pass of a selection (see team_radix_select): keys fall in bins
+  // floor((v - sel_lo) * sel_scale) of their first word's value v.  With
+  // sel_in_bin set, keys above bin sel_bin are taken, keys below it are not,
+  // and the bit-level threshold above decides among the keys in it.
+  double sel_lo, sel_scale;
+  uint32_t sel_bin;
+  int sel_in_bin;
+  int sel_value;  // the selection starts with a value pass
+  int sel_next;   // first key bit of the bit passes after the value pass
 };
 // hist is read as uint4, super and part as uint2 (also over DSMEM).
 static_assert(offsetof(LocalState, hist) % 16 == 0 && (sizeof(uint32_t) * kRadixBins) % 16 == 0,
@@ -836,11 +847,49 @@ __device__ void expand_branch(const Ctx &c, const BranchTable &bt) {
   }
 }
 
-// Counts `key` in its bin of the current pass if it matches the prefix.
-__device__ __forceinline__ void hist_add(const Key3 &key, const Key3 &P, const Key3 &M, int from_top, int width,
-                                         uint32_t *hist) {
-  if ((key.w[0] & M.w[0]) == P.w[0] && (key.w[1] & M.w[1]) == P.w[1] && (key.w[2] & M.w[2]) == P.w[2])
-    atomicAdd(&hist[key_bits(key, from_top, width)], 1u);
+// The f64 whose orderable() image is w0 (-0.0 comes back as +0.0).
+__device__ __forceinline__ double key_value(uint64_t w0) {
+  const uint64_t u = (w0 >> 63) ? (w0 & 0x7FFFFFFFFFFFFFFFull) : ~w0;
+  return __longlong_as_double((long long)u);
+}
+
+// Bin of `key` in a value pass: floor((v - lo) * scale) of its first word's
+// value, clamped to the radix bins.  Non-decreasing in the key.  Rounded
+// explicitly (no fused multiply-add), so that every thread that bins the same
+// key gets the same bin.
+__device__ __forceinline__ uint32_t value_bin(const Key3 &key, double lo, double scale) {
+  const double x = __dmul_rn(__dsub_rn(key_value(key.w[0]), lo), scale);
+  if (!(x >= 0.0)) return 0;
+  if (x >= (double)(kRadixBins - 1)) return kRadixBins - 1;
+  return (uint32_t)x;
+}
+
+constexpr int kPassBits = 0;       // `width` key bits at `from_top`, keys matching P under M
+constexpr int kPassValue = 1;      // value bins of every key
+constexpr int kPassBitsInBin = 2;  // as kPassBits, among the keys in value bin `bin`
+// Value passes are used when the keys share fewer leading bits than this:
+// then a bit pass would mostly separate binades (sign and exponent bits).
+constexpr int kValuePassMaxCommon = 24;
+
+// One radix pass of a selection.
+struct RadixPass {
+  Key3 P, M;
+  int from_top, width;
+  int kind;
+  uint32_t bin;
+  double lo, scale;
+};
+
+// Counts `key` in its bin of the current pass if it takes part in it.
+__device__ __forceinline__ void hist_add(const Key3 &key, const RadixPass &rp, uint32_t *hist) {
+  if (rp.kind == kPassValue) {
+    atomicAdd(&hist[value_bin(key, rp.lo, rp.scale)], 1u);
+    return;
+  }
+  if ((key.w[0] & rp.M.w[0]) == rp.P.w[0] && (key.w[1] & rp.M.w[1]) == rp.P.w[1] &&
+      (key.w[2] & rp.M.w[2]) == rp.P.w[2] &&
+      (rp.kind != kPassBitsInBin || value_bin(key, rp.lo, rp.scale) == rp.bin))
+    atomicAdd(&hist[key_bits(key, rp.from_top, rp.width)], 1u);
 }
 
 // ------------------------------------------------------------- selection
@@ -853,13 +902,23 @@ __device__ __forceinline__ void hist_add(const Key3 &key, const Key3 &P, const K
 // parallel), warp 0 sums and scans them; then the same for the 32 bins of the
 // super-bin that holds the rem-th key.  Nothing is merged with atomics.
 // `start` leading bits of the first key word are common to all n keys (equal
-// to those of common_hi << 32).  On return every CTA's LocalState holds the
+// to those of common_hi << 32); the top 32 bits of every first key word lie
+// in [common_hi, key_hi].  On return every CTA's LocalState holds the
 // threshold: with sel_ge every key >= sel_prefix is taken (exactly k of them),
 // otherwise keys > sel_prefix plus sel_rem keys equal to it.
-// `add_keys(P, M, from_top, width, hist)` histograms (hist_add) this
-// thread's keys, from memory or from registers.
+// With `value_first` and a short common prefix, the first pass is a value
+// pass: 2048 bins linear in the first word's value over the keys' range, so
+// that the threshold bin usually holds a few keys (a bit pass there would
+// mostly separate binades).  When that bin holds exactly the keys still
+// needed, the selection ends; otherwise bit passes continue among the keys of
+// that bin, from the leading bits its value range shares (the range is
+// widened by a whole bin on each side, far beyond the rounding of the bin
+// arithmetic, which is below 2^-40 of a bin here).
+// `add_keys(pass, hist)` histograms (hist_add) this thread's keys, from
+// memory or from registers.
 template <class AddKeys>
-__device__ void team_radix_select(const Ctx &c, uint32_t k, int start, uint32_t common_hi, AddKeys &&add_keys) {
+__device__ void team_radix_select(const Ctx &c, uint32_t k, int start, uint32_t common_hi, uint32_t key_hi,
+                                  bool value_first, AddKeys &&add_keys) {
   LocalState *S = c.S;
   const uint32_t cs = c.cs;
   cg::cluster_group cluster = cg::this_cluster();
@@ -871,15 +930,40 @@ __device__ void team_radix_select(const Ctx &c, uint32_t k, int start, uint32_t 
     S->sel_mask = Key3{{m0, 0, 0}};
     S->sel_rem = k;
     S->sel_ge = 0;
+    S->sel_in_bin = 0;
+    S->sel_value = 0;
+    S->sel_bin = 0;
+    S->sel_lo = 0.0;
+    S->sel_scale = 0.0;
+    if (value_first && start < kValuePassMaxCommon) {
+      // Every key's value lies in [lo, hi] (orderable() is monotone).
+      const double lo = key_value((uint64_t)common_hi << 32);
+      const double hi = key_value(((uint64_t)key_hi << 32) | 0xFFFFFFFFull);
+      const double scale = (double)kRadixBins / (hi - lo);
+      if (hi > lo && scale > 0.0 && scale < 1e300) {
+        S->sel_lo = lo;
+        S->sel_scale = scale;
+        S->sel_value = 1;
+      }
+    }
   }
   __syncthreads();
-  for (int from_top = start; from_top < kKeyBits; from_top += kRadixBits) {
-    const int width = min(kRadixBits, kKeyBits - from_top);
+  bool value = S->sel_value != 0;
+  for (int from_top = start; value || from_top < kKeyBits;) {
+    const int width = value ? kRadixBits : min(kRadixBits, kKeyBits - from_top);
     const uint32_t buf = S->pass & 1u;
     uint32_t *hist = S->hist[buf];
     uint32_t *super = S->super[buf];
-    const Key3 P = S->sel_prefix, M = S->sel_mask;
-    add_keys(P, M, from_top, width, hist);
+    RadixPass rp;
+    rp.P = S->sel_prefix;
+    rp.M = S->sel_mask;
+    rp.from_top = from_top;
+    rp.width = width;
+    rp.kind = value ? kPassValue : (S->sel_in_bin ? kPassBitsInBin : kPassBits);
+    rp.bin = S->sel_bin;
+    rp.lo = S->sel_lo;
+    rp.scale = S->sel_scale;
+    add_keys(rp, hist);
     __syncthreads();
     {
       // Super-bin sums: thread i sums bins 4i..4i+3; 8 lanes make a super-bin.
@@ -977,6 +1061,25 @@ __device__ void team_radix_select(const Ctx &c, uint32_t k, int start, uint32_t 
           // was wrong.  Report it and take everything at or above the prefix.
           atomicOr(c.p->status, kStatusSelection);
           S->sel_ge = 1;
+        } else if (value) {
+          S->sel_in_bin = 1;
+          S->sel_bin = digit;
+          S->sel_rem = rem - above;
+          if (count == S->sel_rem) {
+            // Every key of the bin is taken.
+            S->sel_ge = 1;
+            S->sel_prefix = Key3{{0, 0, 0}};
+            S->sel_mask = Key3{{0, 0, 0}};
+          } else {
+            const double w = 1.0 / S->sel_scale;
+            const uint64_t a = orderable(S->sel_lo + ((double)digit - 1.0) * w);
+            const uint64_t b = orderable(S->sel_lo + ((double)digit + 2.0) * w);
+            const int s2 = a == b ? 64 : __clzll((long long)(a ^ b));
+            const uint64_t m = s2 == 0 ? 0ull : (s2 >= 64 ? ~0ull : ~0ull << (64 - s2));
+            S->sel_prefix = Key3{{a & m, 0, 0}};
+            S->sel_mask = Key3{{m, 0, 0}};
+            S->sel_next = s2;
+          }
         } else {
           S->sel_rem = rem - above;
           key_set_bits(S->sel_prefix, from_top, width, digit);
@@ -987,12 +1090,22 @@ __device__ void team_radix_select(const Ctx &c, uint32_t k, int start, uint32_t 
     }
     __syncthreads();
     if (S->sel_ge) break;
+    if (value) {
+      from_top = S->sel_next;
+      value = false;
+    } else {
+      from_top += kRadixBits;
+    }
   }
 }
 
 // Is `key` among the selected?  Equal keys beyond the threshold count are
 // indistinguishable beams, so which of them are taken does not matter.
 __device__ __forceinline__ bool is_selected(const Ctx &c, const Key3 &key, uint32_t *eq_taken) {
+  if (c.S->sel_in_bin) {
+    const uint32_t b = value_bin(key, c.S->sel_lo, c.S->sel_scale);
+    if (b != c.S->sel_bin) return b > c.S->sel_bin;
+  }
   const int r = key_cmp(key, c.S->sel_prefix);
   if (c.S->sel_ge) return r >= 0;  // the prefix has its free bits at zero
   if (r > 0) return true;
@@ -1066,20 +1179,17 @@ __device__ void materialize_next(const Ctx &c, uint32_t n, uint32_t k, Beam *out
       v = ld_cand(next + i);
       key = cand_key(v, f, depth);
     }
-    team_radix_select(c, k, start, c.S->key_min,
-                      [&](const Key3 &P, const Key3 &M, int from_top, int width, uint32_t *h) {
-                        if (have) hist_add(key, P, M, from_top, width, h);
-                      });
+    team_radix_select(c, k, start, c.S->key_min, c.S->key_max, true, [&](const RadixPass &rp, uint32_t *h) {
+      if (have) hist_add(key, rp, h);
+    });
     if (have && is_selected(c, key, &c.cnt->eq_taken)) take_beam(c, v, k, out_beams, hist);
     return;
   }
   const bool all = n <= k;
   if (!all)
-    team_radix_select(c, k, start, c.S->key_min,
-                      [&](const Key3 &P, const Key3 &M, int from_top, int width, uint32_t *h) {
-                        for (uint32_t i = c.gtid(); i < n; i += c.gthreads())
-                          hist_add(cand_key(ld_cand(next + i), f, depth), P, M, from_top, width, h);
-                      });
+    team_radix_select(c, k, start, c.S->key_min, c.S->key_max, true, [&](const RadixPass &rp, uint32_t *h) {
+      for (uint32_t i = c.gtid(); i < n; i += c.gthreads()) hist_add(cand_key(ld_cand(next + i), f, depth), rp, h);
+    });
   for (uint32_t i = c.gtid(); i < n; i += c.gthreads()) {
     const Cand v = ld_cand(next + i);
     if (!all && !is_selected(c, cand_key(v, f, depth), &c.cnt->eq_taken)) continue;
@@ -1094,11 +1204,11 @@ __device__ void trim_pool(const Ctx &c, uint32_t n, uint32_t k) {
   const double *factor = c.p->factor;
   const uint32_t max_depth = c.step + 1;
   team_radix_select(c, k, common_bits(c.S->pool_key_min, c.S->pool_key_max), c.S->pool_key_min,
-                    [&](const Key3 &P, const Key3 &M, int from_top, int width, uint32_t *h) {
+                    c.S->pool_key_max, true, [&](const RadixPass &rp, uint32_t *h) {
                       for (uint32_t i = c.gtid(); i < n; i += c.gthreads()) {
                         const Cand cv = ld_cand(pool + i);
                         const uint32_t d = min(cv.aux, max_depth);
-                        hist_add(cand_key(cv, factor[d], d), P, M, from_top, width, h);
+                        hist_add(cand_key(cv, factor[d], d), rp, h);
                       }
                     });
   for (uint32_t i = c.gtid(); i < n; i += c.gthreads()) {
