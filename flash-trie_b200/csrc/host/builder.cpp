@@ -32,8 +32,21 @@ struct KeyRef {
   uint32_t terminal;  // node id where the key ends (set by the BFS)
 };
 
-// Lexicographic order on u32 labels, a prefix before its extensions.
-inline bool key_less(const KeyRef &a, const KeyRef &b) {
+// A key while the keys are sorted.  The order is lexicographic on u32
+// labels, a prefix before its extensions.  The first two labels, packed as
+// (l0 << 32) | l1 with zeros where the key is shorter, decide most
+// comparisons without reading the labels: a key shorter than two labels sorts
+// no later than any key with the same packed labels (it is a prefix of them
+// or equal to them), and equal packed labels fall through to the full
+// comparison.
+struct SortKey {
+  uint64_t head;
+  const uint32_t *p;
+  uint32_t len;
+};
+
+inline bool sort_key_less(const SortKey &a, const SortKey &b) {
+  if (a.head != b.head) return a.head < b.head;
   const uint32_t n = std::min(a.len, b.len);
   for (uint32_t i = 0; i < n; ++i)
     if (a.p[i] != b.p[i]) return a.p[i] < b.p[i];
@@ -49,11 +62,14 @@ inline bool key_equal(const KeyRef &a, const KeyRef &b) {
 // it is a suffix of; tail.cc:185-201).
 struct TailEntry {
   const uint32_t *p;  // first label
-  uint32_t len;
+  uint32_t len;       // at least 2: a link spans two or more labels
   uint32_t id;        // index in BFS link order
+  uint64_t last2;     // last two labels, (p[len-1] << 32) | p[len-2]
 };
 
+// Strings whose last two labels differ are ordered by `last2` alone.
 inline bool reversed_less(const TailEntry &a, const TailEntry &b) {
+  if (a.last2 != b.last2) return a.last2 < b.last2;
   const uint32_t n = std::min(a.len, b.len);
   for (uint32_t i = 0; i < n; ++i) {
     const uint32_t x = a.p[a.len - 1 - i], y = b.p[b.len - 1 - i];
@@ -81,16 +97,21 @@ std::unique_ptr<LoudsLevel> build_image(const uint32_t *tokens, const uint64_t *
 
   // ---- 1. sort keys ---------------------------------------------------
   std::vector<KeyRef> keys(num_rows);
-  for (uint64_t i = 0; i < num_rows; ++i) {
-    const uint64_t len = offsets[i + 1] - offsets[i];
-    if (len > 0xFFFFFFFFull) fail(ErrorKind::kSize, "MARISA_SIZE_ERROR: key longer than 2^32-1 labels");
-    keys[i] = KeyRef{tokens + offsets[i], (uint32_t)len, 0};
-  }
-  if (num_threads > 1 && num_rows > 100000) {
-    __gnu_parallel::sort(keys.begin(), keys.end(), key_less,
-                         __gnu_parallel::multiway_mergesort_tag((__gnu_parallel::_ThreadIndex)num_threads));
-  } else {
-    std::sort(keys.begin(), keys.end(), key_less);
+  {
+    std::vector<SortKey> sk(num_rows);
+    for (uint64_t i = 0; i < num_rows; ++i) {
+      const uint64_t len = offsets[i + 1] - offsets[i];
+      if (len > 0xFFFFFFFFull) fail(ErrorKind::kSize, "MARISA_SIZE_ERROR: key longer than 2^32-1 labels");
+      const uint32_t *p = tokens + offsets[i];
+      sk[i] = SortKey{len == 0 ? 0 : ((uint64_t)p[0] << 32) | (len > 1 ? p[1] : 0u), p, (uint32_t)len};
+    }
+    if (num_threads > 1 && num_rows > 100000) {
+      __gnu_parallel::sort(sk.begin(), sk.end(), sort_key_less,
+                           __gnu_parallel::multiway_mergesort_tag((__gnu_parallel::_ThreadIndex)num_threads));
+    } else {
+      std::sort(sk.begin(), sk.end(), sort_key_less);
+    }
+    for (uint64_t i = 0; i < num_rows; ++i) keys[i] = KeyRef{sk[i].p, sk[i].len, 0};
   }
   uint64_t num_unique = num_rows ? 1 : 0;
   for (uint64_t i = 1; i < num_rows; ++i)
@@ -173,7 +194,9 @@ std::unique_ptr<LoudsLevel> build_image(const uint32_t *tokens, const uint64_t *
         bases.push_back(0);
         extras_vals.push_back(0);
         is_link.push_back(1);
-        links.push_back(TailEntry{first.p + w.key_pos, kp - w.key_pos, (uint32_t)links.size()});
+        const uint32_t *lp = first.p + w.key_pos;
+        const uint32_t ll = kp - w.key_pos;
+        links.push_back(TailEntry{lp, ll, (uint32_t)links.size(), ((uint64_t)lp[ll - 1] << 32) | lp[ll - 2]});
       }
       w.key_pos = kp;
       fifo.push_back(w);
