@@ -44,30 +44,48 @@ def bs_tbs_sharded(trie, batch_beams, batch_topk_id, batch_topk_logp, token_logp
     """Searches this rank's slice of the batch with `search` (default
     `flashtrie.bs_tbs_gpu`) and, with `gather`, returns the results of the
     whole batch on every rank: (sents, logp_norms, ms, phase_times), where
-    ms is the slowest rank's call time."""
+    ms is the slowest rank's call time.
+
+    With `gather`, a search that raises on one rank still takes part in the
+    gather (carrying its error instead of results), and then every rank
+    raises: the failing rank its own exception, the others a RuntimeError
+    naming the failed rank.  No rank is left waiting in the collective."""
     if search is None:
         import flashtrie
         search = flashtrie.bs_tbs_gpu
     rank, world = _world(group)
     n = len(batch_beams)
     lo, hi = shard_range(n, rank, world)
-    if hi > lo:
-        sents, lpns, ms, phases = search(trie, hi - lo, batch_beams[lo:hi], batch_topk_id[lo:hi],
-                                         batch_topk_logp[lo:hi], token_logp_threshold, sents_logp_threshold,
-                                         length_norm, early_exit)
-    else:
-        sents, lpns, ms, phases = [], [], 0.0, []
-    local = (list(sents), list(lpns), float(ms), list(phases))
-    if not gather or world == 1:
+    collective = gather and world > 1
+    error, local = None, None
+    try:
+        if hi > lo:
+            sents, lpns, ms, phases = search(trie, hi - lo, batch_beams[lo:hi], batch_topk_id[lo:hi],
+                                             batch_topk_logp[lo:hi], token_logp_threshold, sents_logp_threshold,
+                                             length_norm, early_exit)
+        else:
+            sents, lpns, ms, phases = [], [], 0.0, []
+        local = (list(sents), list(lpns), float(ms), list(phases))
+    except Exception as e:
+        if not collective:
+            raise
+        error = e
+    if not collective:
         return local
     parts = [None] * world
-    dist.all_gather_object(parts, local, group=group)
+    msg = None if error is None else "%s: %s" % (type(error).__name__, error)
+    dist.all_gather_object(parts, (msg, local), group=group)
+    if error is not None:
+        raise error
+    failed = [(r, m) for r, (m, _) in enumerate(parts) if m is not None]
+    if failed:
+        raise RuntimeError("bs_tbs_sharded: the search failed on rank %d (%s)" % failed[0])
     out_s, out_l, out_p = [], [], []
-    for s, l, _, p in parts:
+    for _, (s, l, _, p) in parts:
         out_s.extend(s)
         out_l.extend(l)
         out_p.extend(p)
-    return out_s, out_l, max(p[2] for p in parts), out_p
+    return out_s, out_l, max(part[2] for _, part in parts), out_p
 
 
 def max_over_ranks(values, group=None, device=None):

@@ -87,6 +87,62 @@ def test_sharded_search_gathers_in_request_order(n):
         assert mx == [1.0, 10.0]
 
 
+def failing_search(trie, n, beams, ids, lps, tt, st, ln, ee):
+    """Raises when its slice holds a request marked bad (beam width -1)."""
+    if any(int(b[0]) == -1 for b in beams):
+        raise ValueError("tbs: beam width exceeds max_num_out_beams")
+    return fake_search(trie, n, beams, ids, lps, tt, st, ln, ee)
+
+
+def _failing_worker(rank, world, port, q):
+    import datetime
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        n = 6
+        beams = np.ones((n, 3), dtype=np.int64)
+        beams[n - 1, 0] = -1  # a bad request in the last rank's slice
+        ids = np.zeros((n, 3, 4), dtype=np.uint32)
+        lps = -np.ones((n, 3, 4), dtype=np.float32)
+        try:
+            fs.bs_tbs_sharded(None, beams, ids, lps, -10.0, -40.0, 2.0, False, search=failing_search)
+            q.put((rank, "returned"))
+        except ValueError as e:
+            q.put((rank, "ValueError: %s" % e))
+        except RuntimeError as e:
+            q.put((rank, "RuntimeError: %s" % e))
+        # The group is still usable: every rank took the same collective steps.
+        got = fs.bs_tbs_sharded(None, np.ones((n, 3), dtype=np.int64), ids, lps, -10.0, -40.0, 2.0, False,
+                                search=fake_search)
+        q.put((rank, "after: %d" % len(got[0])))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_search_failure_raises_on_every_rank():
+    """A search that raises on one rank makes every rank raise, with no rank
+    left waiting in the gather: the failing rank its own error, the others a
+    RuntimeError naming it; the process group stays usable."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    res = sorted(q.get(timeout=10) for _ in range(2 * world))
+    assert res == [(0, "RuntimeError: bs_tbs_sharded: the search failed on rank 1 "
+                       "(ValueError: tbs: beam width exceeds max_num_out_beams)"),
+                   (0, "after: 6"),
+                   (1, "ValueError: tbs: beam width exceeds max_num_out_beams"),
+                   (1, "after: 6")], res
+
+
 def test_bench_reference_arm_under_torchrun(tmp_path):
     """Two ranks, CPU: rank 0 alone runs the reference CPU arm and prints one
     JSON line; rank 1 exits 0 without work."""
