@@ -17,7 +17,10 @@ copy in between.  This is the C-ABI entry point `ft_tbs_batch_device`
 
 Inputs (contiguous, on one CUDA device): beams int32 [n, L]; topk_id int32
 [n, L, K] (token ids, read as unsigned); topk_logp float32 [n, L, K].  Rows
-need not be sorted by id.  Outputs: count int32 [n]; logp_norm float64
+need not be sorted by id.  The search runs on `stream` (default: the current
+stream); inputs written on another stream must be ordered before it by the
+caller (an event, or stream.wait_stream), and the outputs are allocated on
+`stream`.  Outputs: count int32 [n]; logp_norm float64
 [n, cap] ascending; lengths int32 [n, cap]; tokens int32 [n, cap, L], beam j
 of request i in tokens[i, j, :lengths[i, j]]; with key_ids=True also key ids
 int32 [n, cap] (LoudsTrie::lookup's id of each result, read as unsigned).
@@ -111,11 +114,16 @@ def bs_tbs_device(trie, beams, topk_id, topk_logp, token_logp_threshold, sents_l
     if capacity is None:
         capacity = int(beams[:, -1].max().item()) if n and L else 1
     capacity = max(int(capacity), 1)
-    count = torch.zeros(n, dtype=torch.int32, device=dev)
-    lpn = torch.empty((n, capacity), dtype=torch.float64, device=dev)
-    lens = torch.zeros((n, capacity), dtype=torch.int32, device=dev)
-    toks = torch.empty((n, capacity, max(L, 1)), dtype=torch.int32, device=dev)
-    keys = torch.full((n, capacity), -1, dtype=torch.int32, device=dev) if key_ids else None
+    if stream is None:
+        stream = torch.cuda.current_stream(dev)
+    # The outputs are allocated and filled on the search's stream, so the
+    # fills come before the search writes them whatever stream is current.
+    with torch.cuda.stream(stream):
+        count = torch.zeros(n, dtype=torch.int32, device=dev)
+        lpn = torch.empty((n, capacity), dtype=torch.float64, device=dev)
+        lens = torch.zeros((n, capacity), dtype=torch.int32, device=dev)
+        toks = torch.empty((n, capacity, max(L, 1)), dtype=torch.int32, device=dev)
+        keys = torch.full((n, capacity), -1, dtype=torch.int32, device=dev) if key_ids else None
     out = (count, lpn, lens, toks) + ((keys,) if key_ids else ())
     if n == 0:
         return out
@@ -123,8 +131,6 @@ def bs_tbs_device(trie, beams, topk_id, topk_logp, token_logp_threshold, sents_l
                lpn.data_ptr(), lens.data_ptr(), toks.data_ptr(), keys.data_ptr() if key_ids else None)
     prm = _Params(float(token_logp_threshold), 0.0, float(sents_logp_threshold), float(length_norm),
                   int(bool(early_exit)), 0)
-    if stream is None:
-        stream = torch.cuda.current_stream(dev)
     with torch.cuda.device(dev):
         _check(_lib().ft_tbs_batch_device(ctypes.c_void_p(trie.ft_handle()), ctypes.byref(b), ctypes.byref(prm),
                                           ctypes.c_void_p(stream.cuda_stream)))
@@ -149,11 +155,12 @@ def lookup(trie, tokens, offsets, stream=None, check=True):
     n = offsets.numel() - 1
     if n < 0:
         raise ValueError("offsets must have n + 1 >= 1 entries")
-    out = torch.empty(n, dtype=torch.int32, device=dev)
-    if n == 0:
-        return out
     if stream is None:
         stream = torch.cuda.current_stream(dev)
+    with torch.cuda.stream(stream):
+        out = torch.empty(n, dtype=torch.int32, device=dev)
+    if n == 0:
+        return out
     with torch.cuda.device(dev):
         _check(_lib().ft_lookup_batch_device(ctypes.c_void_p(trie.ft_handle()), n, ctypes.c_void_p(tokens.data_ptr()),
                                              ctypes.c_void_p(offsets.data_ptr()), tokens.numel(),
@@ -179,12 +186,13 @@ def reverse_lookup(trie, ids, max_len, stream=None, check=True):
     max_len = int(max_len)
     if max_len < 0:
         raise ValueError("max_len must be >= 0")
-    toks = torch.zeros((n, max(max_len, 1)), dtype=torch.int32, device=dev)
-    lens = torch.empty(n, dtype=torch.int32, device=dev)
-    if n == 0:
-        return toks[:, :max_len], lens
     if stream is None:
         stream = torch.cuda.current_stream(dev)
+    with torch.cuda.stream(stream):
+        toks = torch.zeros((n, max(max_len, 1)), dtype=torch.int32, device=dev)
+        lens = torch.empty(n, dtype=torch.int32, device=dev)
+    if n == 0:
+        return toks[:, :max_len], lens
     with torch.cuda.device(dev):
         _check(_lib().ft_reverse_lookup_batch_device(ctypes.c_void_p(trie.ft_handle()), n,
                                                      ctypes.c_void_p(ids.data_ptr()), max_len,

@@ -46,6 +46,34 @@ def test_device_tensors_match_host_path(built, tmp_path):
         assert same_result(d_sents[i], d_lpns[i], h_sents[i], h_lpns[i]), i
 
 
+def test_device_search_on_a_side_stream(built, tmp_path):
+    """A search on a stream other than the current one: its outputs are
+    allocated and cleared on that stream, so it returns what the same search
+    on the current stream returns, twice in a row (the second reuses freed
+    blocks of the first)."""
+    import torch
+    import flashtrie
+    import flashtrie_device as fd
+    p, tok, off, cfg = _trie(tmp_path, seed=23)
+    n = 10
+    beams, ids, lp = W.gen_requests(1, tok, off, n, cfg=cfg)
+    t = flashtrie.Trie()
+    t.load(p)
+    t.init_tbs_gpu(n, max_num_topk=cfg["K"], max_num_outpos=cfg["L"], max_num_out_beams=cfg["beam"])
+    dev = torch.device("cuda:0")
+    d_in = (torch.from_numpy(beams.astype(np.int32)).to(dev), torch.from_numpy(ids.view(np.int32)).to(dev),
+            torch.from_numpy(lp).to(dev))
+    want = fd.to_lists(fd.bs_tbs_device(t, *d_in, -10.0, -40.0, 5.0, False, key_ids=True))
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))  # the inputs were written on the current stream
+    for _ in range(2):
+        out = fd.bs_tbs_device(t, *d_in, -10.0, -40.0, 5.0, False, stream=side, check=False, key_ids=True)
+        side.synchronize()
+        assert fd.device_status(t) == 0
+        assert fd.to_lists(out) == want
+        del out
+
+
 def test_device_tensor_validation(built, tmp_path):
     import torch
     import flashtrie
