@@ -14,7 +14,7 @@
 //      (louds-trie.cc:462-473), label extras, and the node cache
 //      (louds-trie.cc:645-694).
 // The implementation is this project's own: flat index arrays, a vector-backed
-// FIFO, parallel sorts.
+// FIFO, parallel sorts on packed label prefixes, and a parallel tail merge.
 #include <algorithm>
 #include <cfloat>
 #include <cstring>
@@ -233,31 +233,51 @@ std::unique_ptr<LoudsLevel> build_image(const uint32_t *tokens, const uint64_t *
     } else {
       std::sort(sorted.begin(), sorted.end(), reversed_less);
     }
-    std::vector<uint32_t> &buf = lv->tail;
-    const TailEntry *last = nullptr;
-    for (uint64_t i = sorted.size(); i > 0; --i) {
-      const TailEntry &cur = sorted[i - 1];
+    // Walking the sorted strings from the last, each string either shares the
+    // cells of the one walked just before it (when it is a suffix of it) or
+    // is appended to the tail.  Which strings are suffixes of their successor
+    // is decided for all at once; an appended string's position is the total
+    // length appended after it; a suffix lies inside the nearest appended
+    // string after it (suffixes chain), ending where that string ends.
+    const uint64_t m = sorted.size();
+    const uint64_t term = binary ? 0 : 1;
+    std::vector<uint8_t> suffix(m, 0);
+#pragma omp parallel for schedule(static, 4096) num_threads(num_threads)
+    for (int64_t k = 0; k < (int64_t)m - 1; ++k) {
+      const TailEntry &cur = sorted[k], &nx = sorted[k + 1];
       uint32_t match = 0;
-      if (last) {
-        while (match < cur.len && match < last->len &&
-               last->p[last->len - 1 - match] == cur.p[cur.len - 1 - match])
-          ++match;
+      while (match < cur.len && match < nx.len && nx.p[nx.len - 1 - match] == cur.p[cur.len - 1 - match]) ++match;
+      suffix[k] = match == cur.len;
+    }
+    std::vector<uint32_t> pos(m);
+    uint64_t total = 0;
+    for (uint64_t k = m; k > 0; --k) {
+      if (suffix[k - 1]) continue;
+      pos[k - 1] = (uint32_t)total;
+      total += sorted[k - 1].len + term;
+      if (total > 0xFFFFFFFFull) fail(ErrorKind::kSize, "MARISA_SIZE_ERROR: tail exceeds 2^32-1 labels");
+    }
+    {
+      uint64_t owner = m ? m - 1 : 0;
+      for (uint64_t k = m; k > 0; --k) {
+        if (!suffix[k - 1]) owner = k - 1;
+        link_off[sorted[k - 1].id] = (uint32_t)(pos[owner] + sorted[owner].len - sorted[k - 1].len);
       }
-      if (last && match == cur.len) {
-        // `cur` is a suffix of `last`: share its cells.
-        link_off[cur.id] = (uint32_t)(link_off[last->id] + (last->len - match));
-      } else {
-        link_off[cur.id] = (uint32_t)buf.size();
-        buf.insert(buf.end(), cur.p, cur.p + cur.len);
-        if (!binary) {
-          buf.push_back(kTailTerminal);
-        } else {
-          for (uint32_t j = 1; j < cur.len; ++j) lv->tail_end_flags.push_back(false);
-          lv->tail_end_flags.push_back(true);
-        }
-        if (buf.size() > 0xFFFFFFFFull) fail(ErrorKind::kSize, "MARISA_SIZE_ERROR: tail exceeds 2^32-1 labels");
+    }
+    std::vector<uint32_t> &buf = lv->tail;
+    buf.resize(total);
+#pragma omp parallel for schedule(static, 4096) num_threads(num_threads)
+    for (int64_t k = 0; k < (int64_t)m; ++k) {
+      if (suffix[k]) continue;
+      std::memcpy(buf.data() + pos[k], sorted[k].p, 4ull * sorted[k].len);
+      if (!binary) buf[pos[k] + sorted[k].len] = kTailTerminal;
+    }
+    if (binary) {
+      for (uint64_t k = m; k > 0; --k) {
+        if (suffix[k - 1]) continue;
+        for (uint32_t j = 1; j < sorted[k - 1].len; ++j) lv->tail_end_flags.push_back(false);
+        lv->tail_end_flags.push_back(true);
       }
-      last = &cur;
     }
   }
 
