@@ -218,11 +218,16 @@ std::unique_ptr<LoudsLevel> build_image(const uint32_t *tokens, const uint64_t *
   keys = std::vector<KeyRef>();
 
   // ---- 4. tail of link strings --------------------------------------------
+  // A link string holding the text terminator needs a binary tail.
   bool binary = false;
-  for (const TailEntry &e : links) {
-    for (uint32_t i = 0; i < e.len && !binary; ++i)
-      if (e.p[i] == kTailTerminal) binary = true;
-    if (binary) break;
+#pragma omp parallel for schedule(static, 4096) num_threads(num_threads) reduction(|| : binary)
+  for (int64_t k = 0; k < (int64_t)links.size(); ++k) {
+    const TailEntry &e = links[k];
+    for (uint32_t i = 0; i < e.len; ++i)
+      if (e.p[i] == kTailTerminal) {
+        binary = true;
+        break;
+      }
   }
   std::vector<uint32_t> link_off(links.size(), 0);
   {
