@@ -96,7 +96,9 @@ std::unique_ptr<LoudsLevel> build_image(const uint32_t *tokens, const uint64_t *
   if (num_threads < 1) num_threads = 1;
 
   // ---- 1. sort keys ---------------------------------------------------
-  std::vector<KeyRef> keys(num_rows);
+  // Sorted through a temporary array carrying the packed labels; the sorted
+  // keys are allocated after the sort has released its scratch memory.
+  std::vector<KeyRef> keys;
   {
     std::vector<SortKey> sk(num_rows);
     for (uint64_t i = 0; i < num_rows; ++i) {
@@ -111,6 +113,7 @@ std::unique_ptr<LoudsLevel> build_image(const uint32_t *tokens, const uint64_t *
     } else {
       std::sort(sk.begin(), sk.end(), sort_key_less);
     }
+    keys.resize(num_rows);
     for (uint64_t i = 0; i < num_rows; ++i) keys[i] = KeyRef{sk[i].p, sk[i].len, 0};
   }
   uint64_t num_unique = num_rows ? 1 : 0;
