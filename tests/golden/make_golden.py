@@ -23,6 +23,9 @@ Fixtures (JSON):
                 key ids the reference's own lookup tool (tools/marisa-lookup.cc,
                 built by oracle/ref.mk) reports on the config-1 trie for keys,
                 prefixes of keys and random sequences (-1: not a key).
+  search_c2.json
+                config 2's request shape (K=256, L=16, beam 100) on a 200k-key
+                trie of its key distribution: reference CPU `tbs` outputs.
   topk_loader.json
                 a seeded top-k dataset directory (its two text files) and what
                 the reference's `load_topk_keys_and_scores` returns for it.
@@ -35,6 +38,7 @@ The reference never runs on the GPU box; only these files travel.
     python tests/golden/make_golden.py lookup    # lookup_c1.json only
     python tests/golden/make_golden.py topk      # topk_loader.json only
     python tests/golden/make_golden.py api       # api_surface.json only
+    python tests/golden/make_golden.py c2        # search_c2.json only
 """
 import hashlib
 import json
@@ -158,6 +162,35 @@ def topk_loader_golden():
                    "ref_scores": scores}, f)
 
 
+C2_KEYS = 200_000
+C2_REQUESTS = 48
+
+
+def c2_golden():
+    """Config 2's request shape (K=256, L=16, beam 100, V=500k, Zipf 1.05
+    keys of 3-16 labels) on a 200k-key trie of its key distribution: the
+    reference CPU `tbs` output for seeded requests."""
+    import flashtrie_ref as ref
+    from oracle.oracle import OracleTrie
+    cfg = dict(W.CONFIGS[2], keys=C2_KEYS)
+    tok, off = W.gen_keys(cfg["keys"], cfg["vocab"], cfg["len_lo"], cfg["len_hi"], cfg["zipf"], seed=2)
+    t = ref.Trie()
+    t.build(token_rows=W.key_rows(tok, off))
+    path = "/tmp/golden_c2.bin"
+    t.save(path)
+    orc = OracleTrie(path)
+    beams, ids, lp = W.gen_requests(2, tok, off, C2_REQUESTS, cfg=cfg)
+    reqs = []
+    for r in range(C2_REQUESTS):
+        sent, lpn, _ = ref.tbs(t, beams[r].tolist(), ids[r].tolist(), lp[r].tolist(), *THR, False, False)
+        invalid = [i for i, s in enumerate(sent) if not orc.lookup(s)]
+        reqs.append({"index": r, "inputs_sha256": sha(beams[r], ids[r], lp[r]), "ref_sent": sent, "ref_lpn": lpn,
+                     "ref_invalid": invalid})
+    with open(os.path.join(HERE, "search_c2.json"), "w") as f:
+        json.dump({"config": 2, "keys": C2_KEYS, "key_seed": 2, "keys_sha256": sha(tok, off),
+                   "trie_sha256": file_sha(path), "thresholds": THR, "requests": reqs}, f)
+
+
 def api_golden():
     """The first (signature) line of every public function and Trie method's
     docstring in the reference module, as pybind11 writes it."""
@@ -262,9 +295,12 @@ if __name__ == "__main__":
         topk_loader_golden()
     elif sys.argv[1:] == ["api"]:
         api_golden()
+    elif sys.argv[1:] == ["c2"]:
+        c2_golden()
     else:
         main()
         _, tok, off, path = c1_reference_trie()
         lookup_golden(tok, off, path)
         topk_loader_golden()
         api_golden()
+        c2_golden()

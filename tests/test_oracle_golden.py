@@ -81,6 +81,39 @@ def test_oracle_matches_reference_cpu_hand(built, tmp_path):
     print("hand: %d identical, %d explained" % (exact, explained))
 
 
+def test_oracle_matches_reference_cpu_c2_shape(built, tmp_path):
+    """Config 2's request shape (K=256, L=16, beam 100) on a 200k-key trie of
+    its key distribution: the oracle against the reference CPU `tbs`, request
+    by request, under the same rules as config 1."""
+    import flashtrie
+    from oracle.oracle import OracleTrie
+    g = load_json("search_c2.json")
+    cfg = dict(W.CONFIGS[2], keys=g["keys"])
+    tok, off = W.gen_keys(cfg["keys"], cfg["vocab"], cfg["len_lo"], cfg["len_hi"], cfg["zipf"], seed=g["key_seed"])
+    assert sha(tok, off) == g["keys_sha256"], "key generator drifted"
+    t = flashtrie.Trie()
+    t.build(token_rows=W.key_rows(tok, off))
+    p = str(tmp_path / "c2.bin")
+    t.save(p)
+    assert file_sha(p) == g["trie_sha256"], "builder output differs from the reference trie"
+    o = OracleTrie(p)
+    reqs = g["requests"]
+    beams, ids, lp = W.gen_requests(2, tok, off, len(reqs), cfg=cfg)
+    exact = 0
+    for r in reqs:
+        i = r["index"]
+        assert sha(beams[i], ids[i], lp[i]) == r["inputs_sha256"], "request generator drifted"
+        sent, lpn, st = o.tbs(beams[i], ids[i], lp[i], *g["thresholds"], False, stats=True)
+        if same_result(sent, lpn, r["ref_sent"], r["ref_lpn"]):
+            exact += 1
+        else:
+            assert r["ref_invalid"] or st.ties_at_cut > 0, "unexplained difference on request %d" % i
+    # No request of this fixture returns a non-key from the reference CPU or
+    # has equal scores at a selection cut: every one is identical.
+    assert exact == len(reqs)
+    print("c2 shape: %d of %d identical" % (exact, len(reqs)))
+
+
 def test_oracle_key_ids_match_reference_lookup(c1_trie):
     """Key ids (rank of the terminal node) against the reference's own lookup
     tool on the same trie bytes: keys, prefixes of keys, random sequences."""
