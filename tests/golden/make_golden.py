@@ -23,9 +23,10 @@ Fixtures (JSON):
                 key ids the reference's own lookup tool (tools/marisa-lookup.cc,
                 built by oracle/ref.mk) reports on the config-1 trie for keys,
                 prefixes of keys and random sequences (-1: not a key).
-  search_c2.json
-                config 2's request shape (K=256, L=16, beam 100) on a 200k-key
-                trie of its key distribution: reference CPU `tbs` outputs.
+  search_c2.json, search_c3.json
+                the request shapes of configs 2 (K=256, L=16, beam 100) and 3
+                (K=1000, L=20, beam 1000) on 200k-key tries of their key
+                distributions: reference CPU `tbs` outputs.
   topk_loader.json
                 a seeded top-k dataset directory (its two text files) and what
                 the reference's `load_topk_keys_and_scores` returns for it.
@@ -38,7 +39,7 @@ The reference never runs on the GPU box; only these files travel.
     python tests/golden/make_golden.py lookup    # lookup_c1.json only
     python tests/golden/make_golden.py topk      # topk_loader.json only
     python tests/golden/make_golden.py api       # api_surface.json only
-    python tests/golden/make_golden.py c2        # search_c2.json only
+    python tests/golden/make_golden.py shape [2 3]  # search_c2.json / search_c3.json only
 """
 import hashlib
 import json
@@ -162,32 +163,34 @@ def topk_loader_golden():
                    "ref_scores": scores}, f)
 
 
-C2_KEYS = 200_000
-C2_REQUESTS = 48
+# Request shapes of configs 2 and 3 on 200k-key tries of their key
+# distributions: (config, keys, requests, fixture).
+SHAPES = {2: (200_000, 48, "search_c2.json"), 3: (200_000, 24, "search_c3.json")}
 
 
-def c2_golden():
-    """Config 2's request shape (K=256, L=16, beam 100, V=500k, Zipf 1.05
-    keys of 3-16 labels) on a 200k-key trie of its key distribution: the
-    reference CPU `tbs` output for seeded requests."""
+def shape_golden(cfg_id):
+    """A configuration's request shape (its K, L, beam, vocabulary and key
+    distribution) on a 200k-key trie: the reference CPU `tbs` output for
+    seeded requests."""
     import flashtrie_ref as ref
     from oracle.oracle import OracleTrie
-    cfg = dict(W.CONFIGS[2], keys=C2_KEYS)
-    tok, off = W.gen_keys(cfg["keys"], cfg["vocab"], cfg["len_lo"], cfg["len_hi"], cfg["zipf"], seed=2)
+    n_keys, n_req, name = SHAPES[cfg_id]
+    cfg = dict(W.CONFIGS[cfg_id], keys=n_keys)
+    tok, off = W.gen_keys(cfg["keys"], cfg["vocab"], cfg["len_lo"], cfg["len_hi"], cfg["zipf"], seed=cfg_id)
     t = ref.Trie()
     t.build(token_rows=W.key_rows(tok, off))
-    path = "/tmp/golden_c2.bin"
+    path = "/tmp/golden_c%d.bin" % cfg_id
     t.save(path)
     orc = OracleTrie(path)
-    beams, ids, lp = W.gen_requests(2, tok, off, C2_REQUESTS, cfg=cfg)
+    beams, ids, lp = W.gen_requests(cfg_id, tok, off, n_req, cfg=cfg)
     reqs = []
-    for r in range(C2_REQUESTS):
+    for r in range(n_req):
         sent, lpn, _ = ref.tbs(t, beams[r].tolist(), ids[r].tolist(), lp[r].tolist(), *THR, False, False)
         invalid = [i for i, s in enumerate(sent) if not orc.lookup(s)]
         reqs.append({"index": r, "inputs_sha256": sha(beams[r], ids[r], lp[r]), "ref_sent": sent, "ref_lpn": lpn,
                      "ref_invalid": invalid})
-    with open(os.path.join(HERE, "search_c2.json"), "w") as f:
-        json.dump({"config": 2, "keys": C2_KEYS, "key_seed": 2, "keys_sha256": sha(tok, off),
+    with open(os.path.join(HERE, name), "w") as f:
+        json.dump({"config": cfg_id, "keys": n_keys, "key_seed": cfg_id, "keys_sha256": sha(tok, off),
                    "trie_sha256": file_sha(path), "thresholds": THR, "requests": reqs}, f)
 
 
@@ -295,12 +298,14 @@ if __name__ == "__main__":
         topk_loader_golden()
     elif sys.argv[1:] == ["api"]:
         api_golden()
-    elif sys.argv[1:] == ["c2"]:
-        c2_golden()
+    elif sys.argv[1:2] == ["shape"]:
+        for c in sys.argv[2:] or SHAPES:
+            shape_golden(int(c))
     else:
         main()
         _, tok, off, path = c1_reference_trie()
         lookup_golden(tok, off, path)
         topk_loader_golden()
         api_golden()
-        c2_golden()
+        for c in SHAPES:
+            shape_golden(c)

@@ -81,24 +81,26 @@ def test_oracle_matches_reference_cpu_hand(built, tmp_path):
     print("hand: %d identical, %d explained" % (exact, explained))
 
 
-def test_oracle_matches_reference_cpu_c2_shape(built, tmp_path):
-    """Config 2's request shape (K=256, L=16, beam 100) on a 200k-key trie of
-    its key distribution: the oracle against the reference CPU `tbs`, request
-    by request, under the same rules as config 1."""
+@pytest.mark.parametrize("cfg_id", [2, 3])
+def test_oracle_matches_reference_cpu_config_shapes(built, tmp_path, cfg_id):
+    """The request shapes of config 2 (K=256, L=16, beam 100) and config 3
+    (K=1000, L=20, beam 1000) on 200k-key tries of their key distributions:
+    the oracle against the reference CPU `tbs`, request by request, under the
+    same rules as config 1."""
     import flashtrie
     from oracle.oracle import OracleTrie
-    g = load_json("search_c2.json")
-    cfg = dict(W.CONFIGS[2], keys=g["keys"])
+    g = load_json("search_c%d.json" % cfg_id)
+    cfg = dict(W.CONFIGS[cfg_id], keys=g["keys"])
     tok, off = W.gen_keys(cfg["keys"], cfg["vocab"], cfg["len_lo"], cfg["len_hi"], cfg["zipf"], seed=g["key_seed"])
     assert sha(tok, off) == g["keys_sha256"], "key generator drifted"
     t = flashtrie.Trie()
     t.build(token_rows=W.key_rows(tok, off))
-    p = str(tmp_path / "c2.bin")
+    p = str(tmp_path / "shape.bin")
     t.save(p)
     assert file_sha(p) == g["trie_sha256"], "builder output differs from the reference trie"
     o = OracleTrie(p)
     reqs = g["requests"]
-    beams, ids, lp = W.gen_requests(2, tok, off, len(reqs), cfg=cfg)
+    beams, ids, lp = W.gen_requests(cfg_id, tok, off, len(reqs), cfg=cfg)
     exact = 0
     for r in reqs:
         i = r["index"]
@@ -108,10 +110,10 @@ def test_oracle_matches_reference_cpu_c2_shape(built, tmp_path):
             exact += 1
         else:
             assert r["ref_invalid"] or st.ties_at_cut > 0, "unexplained difference on request %d" % i
-    # No request of this fixture returns a non-key from the reference CPU or
+    # No request of these fixtures returns a non-key from the reference CPU or
     # has equal scores at a selection cut: every one is identical.
     assert exact == len(reqs)
-    print("c2 shape: %d of %d identical" % (exact, len(reqs)))
+    print("config %d shape: %d of %d identical" % (cfg_id, exact, len(reqs)))
 
 
 def test_oracle_key_ids_match_reference_lookup(c1_trie):
