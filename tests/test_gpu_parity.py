@@ -59,6 +59,50 @@ def test_c1_single_requests_match_oracle_and_reference(ft, c1):
     assert ref_exact >= 119
 
 
+def check_config_shape(search, tmp_path, cfg_id):
+    """The request shape of config `cfg_id` on the 200k-key trie of its
+    golden fixture: `search(trie_path, beams, ids, lp, thresholds, cfg)` must
+    return, for every request, exactly the oracle's result and exactly the
+    unmodified reference CPU's (every request of these fixtures is one where
+    the reference paths agree)."""
+    import flashtrie
+    from oracle.oracle import OracleTrie
+    g = load_json("search_c%d.json" % cfg_id)
+    cfg = dict(W.CONFIGS[cfg_id], keys=g["keys"])
+    tok, off = W.gen_keys(cfg["keys"], cfg["vocab"], cfg["len_lo"], cfg["len_hi"], cfg["zipf"], seed=g["key_seed"])
+    t = flashtrie.Trie()
+    t.build_flat(tok, off)
+    p = str(tmp_path / "shape.bin")
+    t.save(p)
+    assert file_sha(p) == g["trie_sha256"]
+    reqs = g["requests"]
+    beams, ids, lp = W.gen_requests(cfg_id, tok, off, len(reqs), cfg=cfg)
+    for r in reqs:
+        assert sha(beams[r["index"]], ids[r["index"]], lp[r["index"]]) == r["inputs_sha256"]
+    sents, lpns = search(p, beams, ids, lp, g["thresholds"], cfg)
+    o = OracleTrie(p)
+    for r in reqs:
+        i = r["index"]
+        o_sent, o_lpn = o.tbs(beams[i], ids[i], lp[i], *g["thresholds"], False)
+        assert same_result(sents[i], lpns[i], o_sent, o_lpn), "request %d differs from the oracle" % i
+        assert same_result(sents[i], lpns[i], r["ref_sent"], r["ref_lpn"]), "request %d differs from the reference" % i
+
+
+@pytest.mark.parametrize("cfg_id", [2, 3])
+def test_config_shapes_match_reference(ft, tmp_path, cfg_id):
+    """Configs 2 and 3's request shapes (K=256, L=16, beam 100; K=1000,
+    L=20, beam 1000), the whole fixture as one batch through bs_tbs_gpu:
+    identical to the oracle and to the reference CPU's own outputs."""
+    def search(path, beams, ids, lp, thr, cfg):
+        t = ft.Trie()
+        t.load(path)
+        n = beams.shape[0]
+        t.init_tbs_gpu(n, max_num_topk=cfg["K"], max_num_outpos=cfg["L"], max_num_out_beams=cfg["beam"])
+        sents, lpns, _, _ = ft.bs_tbs_gpu(t, n, beams, ids, lp, thr[0], thr[1], thr[2], False)
+        return sents, lpns
+    check_config_shape(search, tmp_path, cfg_id)
+
+
 def test_c1_batched_matches_single(ft, c1):
     trie, oracle, tok, off, g = c1
     beams, ids, lp = W.gen_requests(1, tok, off, 16, start=200)
