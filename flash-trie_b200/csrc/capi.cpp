@@ -247,6 +247,8 @@ int ft_tbs_batch_device(ft_trie *trie, const ft_device_batch *batch, const ft_se
   return guarded([&] {
     require_trie(trie);
     if (!batch || !params) ftb::fail(ftb::ErrorKind::kNull, "MARISA_NULL_ERROR: NULL argument");
+    if (const char *field = ftb::missing_device_batch_field(*batch))
+      ftb::fail(ftb::ErrorKind::kNull, std::string("MARISA_NULL_ERROR: device batch field ") + field + " is NULL");
     if (!trie->engine)
       ftb::fail(ftb::ErrorKind::kState, "MARISA_STATE_ERROR: init_tbs_gpu must be called before a GPU search");
     trie->engine->search_device(*batch, *params, static_cast<cudaStream_t>(stream));

@@ -20,14 +20,16 @@
 //     before any stream capture.
 //   * All calls share the one array, and it keeps the last call's contents
 //     (each call clears the status word it reads; everything else is written
-//     before it is read).  The entry point serialises its own calls per device
-//     and synchronises the stream before it returns; calls whose GPU work
+//     before it is read).  The entry point serialises its own calls per device;
+//     every call reads the status word back on the caller's stream and
+//     synchronises that stream before it returns.  Calls whose GPU work
 //     overlapped would race on the array.
 //   * A batch whose scratch would exceed kNoAllocScratchBytes is rejected with
 //     FT_ERR_INVALID_ARG; every beam width must be at most out_capacity.
 #include <cuda_runtime.h>
 
 #include <cmath>
+#include <cstdio>
 #include <cstring>
 #include <memory>
 #include <mutex>
@@ -41,6 +43,7 @@
 namespace ftb {
 std::shared_ptr<DeviceTrie> device_trie_of(ft_trie *t);
 void set_last_error(const std::string &m);
+const char *missing_device_batch_field(const ft_device_batch &b);
 }  // namespace ftb
 
 namespace {
@@ -142,6 +145,10 @@ extern "C" int ft_tbs_batch_device_noalloc(ft_trie *trie, const ft_device_batch 
       ftb::set_last_error("MARISA_NULL_ERROR: NULL argument");
       return FT_ERR_NULL;
     }
+    if (const char *field = ftb::missing_device_batch_field(*b)) {
+      ftb::set_last_error(std::string("MARISA_NULL_ERROR: device batch field ") + field + " is NULL");
+      return FT_ERR_NULL;
+    }
     std::shared_ptr<ftb::DeviceTrie> dt = ftb::device_trie_of(trie);
     if (!dt) {
       ftb::set_last_error("MARISA_STATE_ERROR: upload the trie with init_tbs_gpu before searching");
@@ -213,11 +220,15 @@ extern "C" int ft_tbs_batch_device_noalloc(ft_trie *trie, const ft_device_batch 
     const ftb::SearchLaunch plan = ftb::plan_search(n, smem);
     const int grid = (int)std::min<uint32_t>(std::min<uint32_t>(n_slots, (uint32_t)max_ctas), (uint32_t)plan.max_teams);
     ftb::launch_search(sp, smem, grid, stream, plan);
-    CUDA_TRY(cudaStreamSynchronize(stream));
+    // The status word comes back on the caller's stream (pageable
+    // destination: the copy completes before the synchronisation returns).
     uint32_t status = 0;
-    CUDA_TRY(cudaMemcpy(&status, base + a.status, 4, cudaMemcpyDeviceToHost));
+    CUDA_TRY(cudaMemcpyAsync(&status, base + a.status, 4, cudaMemcpyDeviceToHost, stream));
+    CUDA_TRY(cudaStreamSynchronize(stream));
     if (status != 0) {
-      ftb::set_last_error("no-allocation search: the kernel reported status 0x" + std::to_string(status) +
+      char hex[16];
+      std::snprintf(hex, sizeof(hex), "%x", status);
+      ftb::set_last_error(std::string("no-allocation search: the kernel reported status 0x") + hex +
                           " (a beam width above out_capacity, or an inconsistent trie image)");
       return FT_ERR_DEVICE;
     }

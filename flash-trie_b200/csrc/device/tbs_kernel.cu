@@ -667,7 +667,13 @@ __device__ __forceinline__ void task_hash(const Ctx &c, uint32_t base, uint32_t 
   const TrieView &t = c.p->trie;
   const double tt = c.p->token_threshold, st = c.p->sent_threshold;
   const uint32_t lane = threadIdx.x & 31;
-  const uint32_t mask = (1u << lg) - 1u;
+  const uint32_t size = 1u << lg, mask = size - 1u;
+  // The table must lie inside the hash array (base and lg are the same for
+  // the whole warp's task, so the early return is warp-uniform).
+  if (lg > 31 || (uint64_t)base + size > t.hash_slots) {
+    if (lane == 0) atomicOr(c.p->status, kStatusNodeBounds);
+    return;
+  }
   uint32_t x[kItemsPerLane], h[kItemsPerLane], child[kItemsPerLane];
   uint4 rec[kItemsPerLane];
   uint2 slot[kItemsPerLane];
@@ -695,11 +701,22 @@ __device__ __forceinline__ void task_hash(const Ctx &c, uint32_t base, uint32_t 
     if (!on[k]) continue;
     uint2 sl = slot[k];
     uint32_t hk = h[k];
-    while (sl.y != 0 && sl.x != x[k]) {
+    // Load <= 1/2 means an empty slot ends every probe of a valid table; a
+    // full table (an inconsistent image) ends after `size` probes instead.
+    for (uint32_t probe = 1; sl.y != 0 && sl.x != x[k]; ++probe) {
+      if (probe >= size) {
+        atomicOr(c.p->status, kStatusNodeBounds);
+        sl.y = 0;
+        break;
+      }
       hk = (hk + 1) & mask;
       sl = __ldg(t.hash + base + hk);
     }
     child[k] = sl.y;
+    if ((uint64_t)child[k] >= t.num_nodes) {
+      atomicOr(c.p->status, kStatusNodeBounds);
+      child[k] = 0;
+    }
     if (child[k] != 0) rec[k] = __ldg(t.node + child[k]);
   }
   emit_task(c, score, parent_idx, child, rec, [&](auto &&fn) {

@@ -271,6 +271,18 @@ void Engine::search_host(const ft_request *reqs, uint32_t n, const ft_search_par
   }
 }
 
+const char *missing_device_batch_field(const ft_device_batch &b) {
+  if (b.n == 0) return nullptr;
+  if (!b.beams) return "beams";
+  if (b.topk && !b.topk_id) return "topk_id";
+  if (b.topk && !b.topk_logp) return "topk_logp";
+  if (!b.out_count) return "out_count";
+  if (!b.out_lpn) return "out_lpn";
+  if (!b.out_len) return "out_len";
+  if (!b.out_tok) return "out_tok";
+  return nullptr;
+}
+
 void Engine::search_device(const ft_device_batch &b, const ft_search_params &prm, cudaStream_t stream) {
   std::lock_guard<std::mutex> lock(mu_);
   if (b.n > lim_.max_batch)

@@ -41,6 +41,12 @@ class InvalidArgument : public std::runtime_error {
   explicit InvalidArgument(const std::string &m) : std::runtime_error(m) {}
 };
 
+// Name of the first device pointer of a non-empty batch that is NULL but
+// must not be (out_key is optional; the rows may be NULL only when K = 0),
+// or nullptr when every required pointer is set.  Both device entry points
+// refuse such a batch before anything is launched.
+const char *missing_device_batch_field(const ft_device_batch &b);
+
 class Engine {
  public:
   Engine(std::shared_ptr<DeviceTrie> trie, const EngineLimits &lim);

@@ -137,6 +137,8 @@ int ft_tbs_batch(ft_trie *trie, const ft_request *requests, uint32_t n,
  *   beams     u32 [n][L]
  *   topk_id   u32 [n][L][K]
  *   topk_logp f32 [n][L][K]
+ * Every pointer of a non-empty batch except out_key must be set (the rows
+ * only when K > 0); a NULL one is refused with FT_ERR_NULL before any launch.
  * Outputs, per request i, with cap = max final beam and stride = L:
  *   out_count u32 [n]            number of beams
  *   out_lpn   f64 [n][cap]       ascending logp_norm
@@ -206,9 +208,9 @@ int ft_trie_device_status(ft_trie *trie, uint32_t *status);
  * ft_tbs_batch_device, with every beam width at most out_capacity.  Batches
  * whose scratch would exceed 8 MiB are rejected with FT_ERR_INVALID_ARG.
  * The first call on a device looks up the array's address; make it before any
- * stream capture.  Calls are serialised per device and return after the
- * stream has finished the search; all calls share the array, so searches
- * whose GPU work overlapped would race.
+ * stream capture.  Calls are serialised per device; each reads the kernel's
+ * status word back on `stream` and synchronises `stream` before it returns.
+ * All calls share the array, so searches whose GPU work overlapped would race.
  */
 int ft_tbs_batch_device_noalloc(ft_trie *trie, const ft_device_batch *batch,
                                 const ft_search_params *params, void *stream);

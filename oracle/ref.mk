@@ -9,7 +9,14 @@
 #
 #   make -f oracle/ref.mk REF=/path/to/reference        (from the repo root)
 #
-# Output: oracle/_ref/flashtrie_ref$(EXT) (git-ignored, travels to the GPU box)
+# REF defaults to $(FT_REFERENCE), the environment variable __graft_entry__
+# and tests/golden/make_golden.py also read.
+#
+# Output (git-ignored, travels to the GPU box):
+#   oracle/_ref/flashtrie_ref$(EXT)  the reference's pybind11 module
+#   oracle/_ref/marisa-lookup        the reference's key-id lookup tool
+#   oracle/_ref/ref_build            oracle/ref_build.cc over the reference's
+#                                    builder (Keyset + Trie::build + save)
 #
 # Flags follow the reference's CMakeLists.txt:21-27 (MARISA_USE_POPCNT,
 # MARISA_USE_BMI2, -mpopcnt -mbmi2) except -march=native, since the module is
@@ -17,7 +24,7 @@
 # the GPU path: without it the device-side select0 would call the host-only
 # table version of select_bit (bit-vector.cc:18-31 vs :33-392).
 
-REF      ?= /root/reference
+REF      ?= $(FT_REFERENCE)
 OUT      := oracle/_ref
 OBJ      := $(OUT)/obj
 PYINC    := $(shell python3 -c "import sysconfig;print(sysconfig.get_paths()['include'])")
@@ -48,7 +55,16 @@ MODULE   := $(OUT)/flashtrie_ref$(EXT)
 LOOKUP   := $(OUT)/marisa-lookup
 TOOL_OBJS := $(OBJ)/tools/marisa-lookup.o $(OBJ)/tools/cmdopt.o
 
-all: $(MODULE) $(LOOKUP)
+# The reference's own builder driven from flat key files (oracle/ref_build.cc):
+# the reference arm of bench.py builds its trie with it.
+REFBUILD := $(OUT)/ref_build
+REFBUILD_OBJ := $(OBJ)/ref_build.o
+
+all: $(MODULE) $(LOOKUP) $(REFBUILD)
+
+ifeq ($(strip $(REF)),)
+$(error REF is empty: pass REF=/path/to/reference or set FT_REFERENCE)
+endif
 
 $(CU_OBJS): $(OBJ)/%.o: $(REF)/%.cc
 	@mkdir -p $(dir $@)
@@ -75,6 +91,13 @@ $(TOOL_OBJS): $(OBJ)/tools/%.o: $(REF)/tools/%.cc
 	$(CXX) $(CXXFLAGS) -I$(REF)/tools -c $< -o $@
 
 $(LOOKUP): $(CU_OBJS) $(CXX_OBJS) $(TOOL_OBJS) $(DLINK)
+	$(CXX) -fopenmp -o $@ $^ -L/usr/local/cuda/lib64 -lcudart -Wl,-rpath,/usr/local/cuda/lib64
+
+$(REFBUILD_OBJ): oracle/ref_build.cc
+	@mkdir -p $(dir $@)
+	$(CXX) $(CXXFLAGS) -c $< -o $@
+
+$(REFBUILD): $(CU_OBJS) $(CXX_OBJS) $(REFBUILD_OBJ) $(DLINK)
 	$(CXX) -fopenmp -o $@ $^ -L/usr/local/cuda/lib64 -lcudart -Wl,-rpath,/usr/local/cuda/lib64
 
 clean:

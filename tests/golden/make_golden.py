@@ -33,7 +33,9 @@ Fixtures (JSON):
   api_surface.json
                 the signature line of every public function and Trie method
                 of the reference module (names, keyword names, defaults).
-The reference never runs on the GPU box; only these files travel.
+This script and the fixture generation run only where the reference sources
+are (the reference's module is built from them by oracle/ref.mk); the GPU-side
+tests read the committed JSON files and never the reference itself.
 
     python tests/golden/make_golden.py           # all fixtures
     python tests/golden/make_golden.py lookup    # lookup_c1.json only

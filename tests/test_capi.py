@@ -50,6 +50,52 @@ def test_host_entry_points_without_gpu(built, tmp_path):
     lib.ft_trie_destroy(h)
 
 
+class _Params(ctypes.Structure):
+    _fields_ = [("token_logp_threshold", ctypes.c_float), ("reserved", ctypes.c_float),
+                ("sent_logp_threshold", ctypes.c_double), ("length_norm", ctypes.c_double),
+                ("early_exit", ctypes.c_int32), ("reserved2", ctypes.c_int32)]
+
+
+_BATCH_PTRS = ("beams", "topk_id", "topk_logp", "out_count", "out_lpn", "out_len", "out_tok", "out_key")
+
+
+class _Batch(ctypes.Structure):
+    _fields_ = [("n", ctypes.c_uint32), ("num_outpos", ctypes.c_uint32), ("topk", ctypes.c_uint32),
+                ("out_capacity", ctypes.c_uint32)] + [(f, ctypes.c_void_p) for f in _BATCH_PTRS]
+
+
+def test_device_entry_points_refuse_null_pointers(built):
+    """Both device entry points refuse a non-empty batch with a NULL required
+    pointer before anything reaches the device (no GPU involved: the checks
+    run on the host and return FT_ERR_NULL first)."""
+    lib = ctypes.CDLL(os.path.join(REPO, "flash-trie_b200", "libftcore.so"))
+    lib.ft_last_error.restype = ctypes.c_char_p
+    h = ctypes.c_void_p()
+    assert lib.ft_trie_create(ctypes.byref(h)) == 0
+    toks = (ctypes.c_uint32 * 5)(1, 2, 3, 1, 2)
+    offs = (ctypes.c_uint64 * 3)(0, 3, 5)
+    assert lib.ft_trie_build(h, toks, offs, ctypes.c_uint64(2)) == 0
+    prm = _Params(-10.0, 0.0, -40.0, 5.0, 0, 0)
+    # Stand-in addresses: never dereferenced, since every call below is
+    # refused on the host before any launch or copy.
+    fake = {f: 0x1000 * (i + 1) for i, f in enumerate(_BATCH_PTRS)}
+    required = [f for f in _BATCH_PTRS if f != "out_key"]
+    for entry in ("ft_tbs_batch_device", "ft_tbs_batch_device_noalloc"):
+        fn = getattr(lib, entry)
+        for missing in required:
+            ptrs = dict(fake, **{missing: None})
+            b = _Batch(2, 3, 4, 8, *[ptrs[f] for f in _BATCH_PTRS])
+            rc = fn(h, ctypes.byref(b), ctypes.byref(prm), None)
+            assert rc == -2, (entry, missing, rc)  # FT_ERR_NULL
+            assert missing.encode() in lib.ft_last_error(), (entry, missing)
+        # An empty batch needs no pointers: nothing to check, nothing to do
+        # (the allocating entry point still needs a workspace first).
+        empty = _Batch(0, 3, 4, 8, *([None] * len(_BATCH_PTRS)))
+        rc = fn(h, ctypes.byref(empty), ctypes.byref(prm), None)
+        assert rc in (0, -1), (entry, rc)
+    lib.ft_trie_destroy(h)
+
+
 def test_device_api_rejects_host_tensors(built):
     """flashtrie_device validates its inputs before touching a device."""
     import pytest

@@ -229,7 +229,7 @@ def test_empty_and_single_key_tries(ft, tmp_path):
         assert same_result(sent, lpn, o_sent, o_lpn), keys
 
 
-def test_device_entry_point_matches_host(ft, c1):
+def test_device_entry_point_matches_host(ft, c1, tmp_path):
     """ft_tbs_batch_device on torch device buffers == the host entry point."""
     import torch
     trie, oracle, tok, off, g = c1
@@ -263,7 +263,7 @@ def test_device_entry_point_matches_host(ft, c1):
     # The Python trie object wraps an ft_trie*; reach it through a fresh C-ABI handle instead.
     h = ctypes.c_void_p()
     assert lib.ft_trie_create(ctypes.byref(h)) == 0
-    path = str(os.path.join("/tmp", "c1_dev.bin"))
+    path = str(tmp_path / "c1_dev.bin")
     trie.save(path)
     assert lib.ft_trie_load(h, path.encode()) == 0
     assert lib.ft_trie_init_tbs_gpu(h, ctypes.c_uint64(n), ctypes.c_uint64(K), ctypes.c_uint64(L),
