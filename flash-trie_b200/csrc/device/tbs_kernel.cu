@@ -1948,16 +1948,21 @@ SearchLaunch plan_search(uint32_t n, size_t smem_bytes) {
   const int sms = sm_count();
   SearchLaunch l;
   int cs = 1;
+  bool forced = false;
   if (const char *e = getenv("FT_CLUSTER_SIZE")) {
     cs = atoi(e);
     if (cs < 1 || cs > 16 || (cs & (cs - 1))) cs = 1;
+    forced = true;
   } else {
     const int want = n ? sms / (int)n : sms;
     while (cs * 2 <= 16 && cs * 2 <= want) cs *= 2;
   }
+  // Halve the team until the whole batch is resident at once: clusters of
+  // 16 CTAs need 16 free SMs of one GPC, so fewer of them fit than SMs / 16,
+  // and a request left for a second wave doubles the batch's time.
   for (;; cs /= 2) {
     const int teams = max_search_clusters(cs, smem_bytes);
-    if (teams >= 1 || cs == 1) {
+    if ((teams >= 1 && (forced || teams >= (int)n)) || cs == 1) {
       l.cluster_size = cs;
       l.max_teams = std::max(teams, 1);
       break;

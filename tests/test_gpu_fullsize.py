@@ -4,7 +4,8 @@ Config 2 is searched at its full size (10M keys, V=500k, K=256, L=16, beam
 100) and compared with the oracle request by request.  Configs 3 and 5 keep
 their request shapes (K=1000, L=20/24, beam 1000, V=2.2M; config 5 with
 early exit and 30% off-trie requests) on a 12M-key trie of their key
-distribution; FT_FULLSIZE=1 adds config 3 at its full 200M keys.
+distribution, and config 3 is also searched at its full 200M keys (16
+requests, every one compared with the oracle).
 
 Besides the direct comparison, every result of every request is checked
 through properties that hold at any size: at most beams[L-1] results, in
@@ -14,8 +15,6 @@ threshold, every prefix score above the sentence threshold, and the score
 recomputed from the proposals (f32 log-probabilities summed in f64, times
 (6/(5+len))^length_norm) equal to the reported one bit for bit.
 """
-import os
-
 import numpy as np
 import pytest
 
@@ -111,7 +110,6 @@ def test_config_shapes_at_12m_keys(tmp_path_factory, built, cfg_id):
     assert total > 0
 
 
-@pytest.mark.skipif(os.environ.get("FT_FULLSIZE") != "1", reason="200M-key trie; set FT_FULLSIZE=1")
 def test_config3_full_size_matches_oracle(tmp_path_factory, built):
     path, tok, off, cfg = _build(tmp_path_factory, 3, W.CONFIGS[3]["keys"], "c3full")
     total = _run(path, tok, off, cfg, 3, n_req=16, n_direct=16)

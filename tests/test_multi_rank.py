@@ -162,3 +162,7 @@ def test_bench_reference_arm_under_torchrun(tmp_path):
     d = json.loads(lines[0])
     assert d["impl"] == "reference" and d["value"] > 0 and d["cpu_baseline"]["kind"] == "reference"
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["n_gpus"] == 2
+    # The arm searched a trie the reference's own builder wrote, and never
+    # loaded the engine.
+    assert d["config"]["trie_built_by"].startswith("reference builder"), d["config"]
+    assert d["engine_modules_loaded"] == [] and d["steps"] == 3

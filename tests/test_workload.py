@@ -70,3 +70,22 @@ def test_target_key_is_proposed():
                 found += 1
                 break
     assert found == 20
+
+
+def test_torch_keys_sorted_and_length_weights():
+    """sort=True returns the same key set in lexicographic order (a key before
+    the keys it prefixes); len_weights draws lengths with those weights
+    before duplicates are dropped."""
+    tok, off = W.gen_keys_torch(4000, 400, 1, 5, 1.0, seed=4, device="cpu", sort=True)
+    rows = [tuple(tok[off[i]:off[i + 1]].tolist()) for i in range(len(off) - 1)]
+    assert rows == sorted(rows) and len(set(rows)) == len(rows) == 4000
+    tok2, off2 = W.gen_keys_torch(4000, 400, 1, 5, 1.0, seed=4, device="cpu")
+    assert sorted(tuple(tok2[off2[i]:off2[i + 1]].tolist()) for i in range(4000)) == rows
+    cfg = W.resolve(4, keys=20000)
+    assert cfg["keyset"] == "ref-lengths" and (cfg["len_lo"], cfg["len_hi"]) == (1, 8)
+    tok3, off3 = W.gen_keys_torch(20000, cfg["vocab"], cfg["len_lo"], cfg["len_hi"], cfg["zipf"], seed=4,
+                                  device="cpu", len_weights=cfg["len_weights"], sort=True)
+    lens = np.bincount(np.diff(off3).astype(np.int64), minlength=9)
+    assert lens[0] == 0 and lens[3] == lens.max()  # length 3 carries the largest weight
+    with pytest.raises(ValueError):
+        W.gen_keys_torch(10, 100, 1, 3, 1.0, seed=1, device="cpu", len_weights=[1, 2])

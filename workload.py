@@ -31,6 +31,35 @@ CONFIGS = {
     5: dict(keys=800_000_000, vocab=2_200_000, len_lo=4, len_hi=24, zipf=1.0, K=1000, L=24, beam=1000,
             batch=64, early_exit=True, off_trie=0.3),
 }
+# Key-length distributions.  "spec" is the configuration's own (uniform in
+# [len_lo, len_hi]).  Configs 4 and 5 as written (800M keys, lengths 4-24)
+# need about 11G tail labels, beyond the 2^32-label tail of the trie format
+# (lib/marisa/grimoire/trie/tail.cc:221), so at 800M keys they use
+# "ref-lengths": lengths 1-8 drawn with the reference's example-generator
+# weights 2,10,45,25,10,5,2,1 (examples/make_example_data.py:57), the
+# distribution behind the reference's 800M-key index figure; vocabulary and
+# Zipf exponent stay the configuration's.
+KEYSETS = {
+    "spec": {},
+    "ref-lengths": dict(len_lo=1, len_hi=8, len_weights=(2, 10, 45, 25, 10, 5, 2, 1)),
+}
+DEFAULT_KEYSET = {1: "spec", 2: "spec", 3: "spec", 4: "ref-lengths", 5: "ref-lengths"}
+
+
+def resolve(cfg_id, keyset=None, **overrides):
+    """The configuration's parameters with its key-length distribution
+    (`keyset`, default per config) and any overrides applied."""
+    cfg = dict(CONFIGS[cfg_id])
+    ks = keyset or DEFAULT_KEYSET[cfg_id]
+    cfg.update(KEYSETS[ks])
+    cfg["keyset"] = ks
+    cfg.setdefault("len_weights", None)
+    for k, v in overrides.items():
+        if v:
+            cfg[k] = v
+    return cfg
+
+
 TOKEN_LOGP_THRESHOLD = -10.0
 SENT_LOGP_THRESHOLD = -40.0
 LENGTH_NORM = 5.0
@@ -163,10 +192,19 @@ def gen_requests(cfg_id, tokens, offsets, n_requests, start=0, cfg=None, root_ch
     return beams, np.stack(out_ids), np.stack(out_lp)
 
 
-def gen_keys_torch(n, vocab, len_lo, len_hi, zipf_s, seed, device="cuda"):
+def gen_keys_torch(n, vocab, len_lo, len_hi, zipf_s, seed, device="cuda", len_weights=None, sort=False):
     """Same distribution as gen_keys, drawn with torch on `device` (seconds for
     10^7-10^8 keys on a GPU instead of minutes with numpy).  Deterministic for
-    a given seed and device type; returns numpy (tokens u32, offsets u64)."""
+    a given seed and device type; returns numpy (tokens u32, offsets u64).
+
+    len_weights: relative frequencies of the lengths len_lo..len_hi instead of
+    a uniform length (the reference's example generator draws lengths 1..8
+    with weights 2,10,45,25,10,5,2,1, examples/make_example_data.py:57);
+    duplicates are dropped after drawing, so short keys end up rarer than
+    their weight where their distinct count runs out.
+    sort: return the keys in lexicographic order (a shorter key before the
+    keys it prefixes), the order every trie builder sorts them into; the
+    key set is the same either way."""
     import torch
     dev = torch.device(device)
     g = torch.Generator(device=dev)
@@ -176,6 +214,11 @@ def gen_keys_torch(n, vocab, len_lo, len_hi, zipf_s, seed, device="cuda"):
     cdf /= cdf[-1].clone()
     width = len_hi
     cols = torch.arange(width, device=dev)
+    if len_weights is not None:
+        lw = torch.tensor([float(x) for x in len_weights], dtype=torch.float64, device=dev)
+        if lw.numel() != len_hi - len_lo + 1 or bool((lw < 0).any()) or float(lw.sum()) <= 0:
+            raise ValueError("len_weights needs one non-negative weight per length %d..%d" % (len_lo, len_hi))
+        lw /= lw.sum()
     mats, lens_l, hashes = [], [], []
     keep = None
     m = int(n * 1.1) + 4096
@@ -183,7 +226,10 @@ def gen_keys_torch(n, vocab, len_lo, len_hi, zipf_s, seed, device="cuda"):
     while True:
         for c0 in range(0, m, chunk):
             mc = min(chunk, m - c0)
-            lens = torch.randint(len_lo, len_hi + 1, (mc,), generator=g, device=dev)
+            if len_weights is None:
+                lens = torch.randint(len_lo, len_hi + 1, (mc,), generator=g, device=dev)
+            else:
+                lens = torch.multinomial(lw, mc, replacement=True, generator=g) + len_lo
             u = torch.rand(mc * width, generator=g, device=dev, dtype=torch.float64)
             mat = torch.searchsorted(cdf, u, right=True).clamp_(max=vocab - 1).view(mc, width)
             del u
@@ -213,6 +259,17 @@ def gen_keys_torch(n, vocab, len_lo, len_hi, zipf_s, seed, device="cuda"):
     mat = allm[keep]
     del allm
     lens = alll[keep].to(torch.int64)
+    if sort:
+        # LSD: stable sorts by column from the last to the first; a position
+        # past a key's end sorts before every token (token + 1 vs 0).
+        perm = torch.arange(n, device=dev)
+        for c in range(width - 1, -1, -1):
+            col = torch.where(lens[perm] > c, mat[perm, c].to(torch.int64) + 1, 0)
+            perm = perm[torch.sort(col, stable=True).indices]
+            del col
+        mat = mat[perm]
+        lens = lens[perm]
+        del perm
     offsets = torch.zeros(n + 1, dtype=torch.int64, device=dev)
     torch.cumsum(lens, 0, out=offsets[1:])
     tokens = mat[cols[None, :] < lens[:, None]]
