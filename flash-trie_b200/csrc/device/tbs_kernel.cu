@@ -91,6 +91,16 @@ __device__ __forceinline__ Key3 cand_key(const Cand &c, double factor, uint32_t 
   return k;
 }
 
+// The same key from a candidate's first 16 bytes (score in .x/.y, node in .z).
+__device__ __forceinline__ Key3 head_key(const uint4 h, double factor, uint32_t depth) {
+  const double score = __hiloint2double((int)h.y, (int)h.x);
+  Key3 k;
+  k.w[0] = orderable(score * factor);
+  k.w[1] = ((uint64_t)h.z << 32) | ((uint64_t)(depth & 0xFFFFu) << 16);
+  k.w[2] = orderable(score);
+  return k;
+}
+
 __device__ __forceinline__ int key_cmp(const Key3 &a, const Key3 &b) {
 #pragma unroll
   for (int i = 0; i < 3; ++i) {
@@ -144,6 +154,24 @@ __device__ __forceinline__ Cand ld_cand(const Cand *p) {
   return c;
 }
 
+// The first 16 bytes of a candidate (score, node, aux): all a selection key
+// needs.  The second half (parent, token, c0, dw) is loaded only for the
+// candidates that are kept.
+__device__ __forceinline__ uint4 ld_cand_head(const Cand *p) { return __ldcg(reinterpret_cast<const uint4 *>(p)); }
+
+__device__ __forceinline__ Cand cand_from(const uint4 a, const Cand *p) {
+  const uint4 b = __ldcg(reinterpret_cast<const uint4 *>(p) + 1);
+  Cand c;
+  c.score = __hiloint2double((int)a.y, (int)a.x);
+  c.node = a.z;
+  c.aux = a.w;
+  c.parent = b.x;
+  c.token = b.y;
+  c.c0 = b.z;
+  c.dw = b.w;
+  return c;
+}
+
 __device__ __forceinline__ Beam ld_beam(const Beam *p) {
   const uint2 *q = reinterpret_cast<const uint2 *>(p);
   const uint2 a = __ldcg(q), b = __ldcg(q + 1), d = __ldcg(q + 2);
@@ -185,7 +213,7 @@ struct StepCounters {
   uint32_t n_in_new;  // ... of which in-link
   uint32_t n_br_new;  // ... of which branching
   uint32_t eq_taken;  // keys equal to the selection threshold taken so far
-  uint32_t pad;
+  uint32_t task_next; // branch tasks handed out (cumulative over the step's chunks)
 };
 
 // Authoritative in the team's rank-0 CTA; other CTAs reach it through
@@ -437,7 +465,13 @@ __device__ void expand_inlink(const Ctx &c) {
   const TrieView &t = c.p->trie;
   const double tt = c.p->token_threshold, st = c.p->sent_threshold;
   const uint32_t n_in = c.S->n_in;
-  for (uint32_t i = c.gtid(); i < n_in; i += c.gthreads()) {
+  // Beam i goes to CTA i % cs, and within it round-robin over the warps
+  // first, so that every warp holds about the same share of this chain of
+  // dependent loads and then takes fewer branch tasks (handed out on demand).
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (uint32_t j = lane * kWarps + warp;; j += blockDim.x) {
+    const uint32_t i = j * c.cs + c.rank;
+    if (i >= n_in) break;
     const Beam b = ld_beam(c.cur + i);
     const uint32_t off = b.off;
     if ((uint64_t)off >= t.tail_size || (uint64_t)b.node >= t.num_nodes) {
@@ -781,12 +815,30 @@ __device__ __forceinline__ void task_bin(const Ctx &c, uint32_t c0, uint32_t d, 
 // of (parent, 128 items) and the team's warps drain it, each task doing its
 // lookups and the gathers of what they found.  A heavy parent is spread over
 // every warp of the team; no team barrier is needed between chunks.
+// Task `task` of the current chunk: its parent (the last one whose first
+// task is <= task).
+__device__ __forceinline__ uint32_t task_parent(const BranchTable &bt, uint32_t m, uint32_t task) {
+  uint32_t lo = 0, n = m;
+  while (n > 1) {
+    const uint32_t half = n >> 1;
+    if (bt.start[lo + half] <= task) {
+      lo += half;
+      n -= half;
+    } else {
+      n = half;
+    }
+  }
+  return lo;
+}
+
 __device__ void expand_branch(const Ctx &c, const BranchTable &bt) {
   const TrieView &t = c.p->trie;
-  const uint32_t warp = threadIdx.x >> 5;
+  const uint32_t lane = threadIdx.x & 31;
   const uint32_t n_br = c.S->n_br;
   const uint32_t K = c.row.K;
   const uint32_t beam_cap = c.p->beam_cap;
+  const uint32_t team_warps = c.cs * kWarps;
+  const uint32_t wid = c.rank * kWarps + (threadIdx.x >> 5);
   for (uint32_t c_first = 0; c_first < n_br; c_first += kParentChunk) {
     const uint32_t m = min(kParentChunk, n_br - c_first);
     uint32_t my_tasks[kParentChunk / kSearchThreads];
@@ -835,18 +887,17 @@ __device__ void expand_branch(const Ctx &c, const BranchTable &bt) {
     if (threadIdx.x == blockDim.x - 1) c.S->n_tasks = pre;
     __syncthreads();
     const uint32_t total = c.S->n_tasks;
-    const uint32_t team_warps = c.cs * kWarps;
-    for (uint32_t task = c.rank * kWarps + warp; task < total; task += team_warps) {
-      uint32_t lo = 0, n = m;  // last parent whose first task <= task
-      while (n > 1) {
-        const uint32_t half = n >> 1;
-        if (bt.start[lo + half] <= task) {
-          lo += half;
-          n -= half;
-        } else {
-          n = half;
-        }
-      }
+    // Every warp runs task `wid` first (no wait).  In the first chunk, tasks
+    // beyond the team's warps are handed out on demand from the team's
+    // counter: a warp asks for its next task before it runs the current one,
+    // so the round trip overlaps the task, and a warp that drew cheap tasks
+    // takes more.  Later chunks (beam widths above 1024) go round-robin.
+    const uint32_t n_dyn = (c_first == 0 && total > team_warps) ? total - team_warps : 0u;
+    uint32_t task = wid;
+    while (task < total) {
+      uint32_t nxt = 0xFFFFFFFFu;
+      if (n_dyn && lane == 0) nxt = atomicAdd(&c.cnt->task_next, 1u);
+      const uint32_t lo = task_parent(bt, m, task);
       const uint4 info = bt.info[lo];
       const double score = bt.score[lo];
       const uint32_t first_item = (task - bt.start[lo]) * kTaskItems;
@@ -858,6 +909,12 @@ __device__ void expand_branch(const Ctx &c, const BranchTable &bt) {
         task_hash(c, info.z, info.w >> 8, first_item, score, parent_idx);
       } else {
         task_bin(c, info.x, info.y, first_item, score, parent_idx);
+      }
+      if (n_dyn) {
+        const uint32_t v = __shfl_sync(0xFFFFFFFFu, nxt, 0);
+        task = v < n_dyn ? team_warps + v : total;
+      } else {
+        task += team_warps;
       }
     }
     __syncthreads();  // the task table is rebuilt for the next chunk
@@ -1203,14 +1260,24 @@ __device__ void materialize_next(const Ctx &c, uint32_t n, uint32_t k, Beam *out
     return;
   }
   const bool all = n <= k;
+  const uint32_t G = c.gthreads();
   if (!all)
     team_radix_select(c, k, start, c.S->key_min, c.S->key_max, true, [&](const RadixPass &rp, uint32_t *h) {
-      for (uint32_t i = c.gtid(); i < n; i += c.gthreads()) hist_add(cand_key(ld_cand(next + i), f, depth), rp, h);
+      // Four candidates' loads in flight before any is counted.
+      uint32_t i = c.gtid();
+      for (; i + 3 * G < n; i += 4 * G) {
+        uint4 a[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) a[u] = ld_cand_head(next + i + u * G);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) hist_add(head_key(a[u], f, depth), rp, h);
+      }
+      for (; i < n; i += G) hist_add(head_key(ld_cand_head(next + i), f, depth), rp, h);
     });
-  for (uint32_t i = c.gtid(); i < n; i += c.gthreads()) {
-    const Cand v = ld_cand(next + i);
-    if (!all && !is_selected(c, cand_key(v, f, depth), &c.cnt->eq_taken)) continue;
-    take_beam(c, v, k, out_beams, hist);
+  for (uint32_t i = c.gtid(); i < n; i += G) {
+    const uint4 a = ld_cand_head(next + i);
+    if (!all && !is_selected(c, head_key(a, f, depth), &c.cnt->eq_taken)) continue;
+    take_beam(c, cand_from(a, next + i), k, out_beams, hist);
   }
 }
 
@@ -1396,6 +1463,7 @@ __device__ void reset_counters(StepCounters *s) {
   s->n_in_new = 0;
   s->n_br_new = 0;
   s->eq_taken = 0;
+  s->task_next = 0;
 }
 
 // One request, searched by the whole team.  Cluster barriers per step: one
