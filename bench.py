@@ -522,6 +522,7 @@ class Device:
         self.lib, self.handle, self.stream, self.prm = lib, handle, stream, prm
         self.R = len(beams)
         self.L, self.K, self.cap = L, K, cap
+        self.out_cap = cap  # the output capacity a call declares: its beam width
         self.d_beams = torch.from_numpy(np.ascontiguousarray(beams).astype(np.int32)).to(dev)
         self.d_ids = torch.from_numpy(np.ascontiguousarray(ids).view(np.int32)).to(dev)
         self.d_lp = torch.from_numpy(np.ascontiguousarray(lp)).to(dev)
@@ -530,6 +531,7 @@ class Device:
 
     def set_beam(self, beam):
         self.d_beams.fill_(int(beam))
+        self.out_cap = min(int(beam), self.cap)
 
     def _outs(self, nb):
         import torch
@@ -546,7 +548,7 @@ class Device:
         resident requests (consecutive batches use different requests)."""
         s = (step * nb) % max(1, self.R - nb + 1) if self.R > nb else 0
         oc, ol, on, ot = self._outs(nb)
-        b = DeviceBatch(nb, self.L, self.K, self.cap, self.d_beams[s].data_ptr(), self.d_ids[s].data_ptr(),
+        b = DeviceBatch(nb, self.L, self.K, self.out_cap, self.d_beams[s].data_ptr(), self.d_ids[s].data_ptr(),
                         self.d_lp[s].data_ptr(), oc.data_ptr(), ol.data_ptr(), on.data_ptr(), ot.data_ptr())
         rc = self.lib.ft_tbs_batch_device(self.handle, ctypes.byref(b), ctypes.byref(self.prm),
                                           ctypes.c_void_p(self.stream.cuda_stream))

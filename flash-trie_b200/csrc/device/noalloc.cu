@@ -117,6 +117,7 @@ __global__ void noalloc_setup_kernel(Layout a, uint32_t n, uint32_t L, uint32_t 
     v.beams[0] = reinterpret_cast<ftb::Beam *>(sb + a.beams0);
     v.beams[1] = reinterpret_cast<ftb::Beam *>(sb + a.beams1);
     v.hist = reinterpret_cast<ftb::Hist *>(sb + a.hist);
+    v.help = nullptr;  // no helper clusters in this search
     slots[s] = v;
   }
   if (threadIdx.x == 0) *reinterpret_cast<uint32_t *>(base + a.status) = 0;  // status starts clean

@@ -43,6 +43,7 @@
 // lookup_kernel (token sequence -> key id) and reverse_lookup_kernel (key id
 // -> token sequence, over parents derived by parents_kernel).
 #include <algorithm>
+#include <atomic>
 #include <cstddef>
 #include <cstdlib>
 #include <map>
@@ -70,6 +71,12 @@ constexpr int kNodeFlagTerminal = 1;
 constexpr int kNodeFlagLink = 2;
 constexpr int kNodeFlagHashed = 4;     // plain nodes
 constexpr int kNodeFlagLinkEnds1 = 4;  // link nodes
+// Bounded waits on helper clusters (on the GPU's global timer), the longest
+// sleep between two polls of a helper waiting for its leader, and the fewest
+// tasks for which a step is opened to helpers.
+constexpr unsigned long long kHelpWaitNs = 20000000ull;  // 20 ms
+constexpr uint32_t kHelpMaxSleepNs = 1024;
+constexpr uint32_t kHelpMinTasks = 1024;
 
 // ------------------------------------------------------------- keys
 // Monotone map of an f64 to u64 (-0.0 folded onto +0.0).
@@ -206,23 +213,21 @@ constexpr uint32_t kMaxTeam = 16;            // CTAs per team (non-portable clus
 // t is read by every CTA after the barrier that closes step t, so the leader
 // clears it again only after the next step's expansion barrier.
 struct StepCounters {
-  uint32_t n_next;    // candidates appended
-  uint32_t key_min;   // range of the top 32 bits of the candidates' first key word
-  uint32_t key_max;
   uint32_t n_sel;     // beams written for the next step (capped at its width)
   uint32_t n_in_new;  // ... of which in-link
   uint32_t n_br_new;  // ... of which branching
   uint32_t eq_taken;  // keys equal to the selection threshold taken so far
-  uint32_t task_next; // branch tasks handed out (cumulative over the step's chunks)
+  uint32_t n_tasks_new;  // branch tasks of the next step, summed from the branching beams' fan-outs
 };
 
 // Authoritative in the team's rank-0 CTA; other CTAs reach it through
 // distributed shared memory.
+// The expansion counters (xc, pool) are used from here in a request without
+// helper clusters, from the slot's HelpState in a request with them.
 struct alignas(16) TeamState {
   StepCounters cnt[2];
-  uint32_t pool_end;       // pool entries (append counter)
-  uint32_t pool_key_min;   // range of the top 32 bits of the pool entries' first key word
-  uint32_t pool_key_max;
+  ExpCounters xc[2];
+  PoolCounters pool;
   uint32_t n_compact;      // entries written by the last pool trim
   uint32_t eq_taken_trim;
   uint32_t pad;
@@ -261,6 +266,12 @@ struct alignas(16) LocalState {
   int sel_in_bin;
   int sel_value;  // the selection starts with a value pass
   int sel_next;   // first key bit of the bit passes after the value pass
+  uint32_t help_step;   // helper CTA: the step it works on next (kHelpStop: none)
+  uint32_t help_epoch;  // the request's helper epoch
+  uint32_t pool_base;   // the pool's end at this step's start
+  uint32_t pool_add;    // added to pool slots from Ctx::xp (an open step appends after pool_base)
+  uint32_t est_tasks;   // this step's branch tasks as the last selection counted them
+  uint32_t help_open;   // this step is shared with helper clusters
 };
 // hist is read as uint4, super and part as uint2 (also over DSMEM).
 static_assert(offsetof(LocalState, hist) % 16 == 0 && (sizeof(uint32_t) * kRadixBins) % 16 == 0,
@@ -296,6 +307,13 @@ struct Ctx {
   double f_next;   // length-norm factor of the candidates' depth (t + 1)
   uint32_t rank;   // CTA rank in the team
   uint32_t cs;     // team size (CTAs)
+  // Counters every expanding CTA appends to (this step's set and the
+  // pool's): in the leader team's shared memory, or in the slot's HelpState
+  // when the request has helper clusters.  help: set while a step is shared
+  // with helpers; T == nullptr on a helper CTA.
+  ExpCounters *xc;
+  PoolCounters *xp;
+  HelpState *help;
   // Ranges of this thread's pushes (top 32 bits of the first key word),
   // folded into the team's at the end of expansion.
   mutable uint32_t kmin, kmax, pkmin, pkmax;
@@ -370,12 +388,12 @@ __device__ __forceinline__ void publish_ranges(const Ctx &c) {
   }
   const uint32_t lane = threadIdx.x & 31;
   if (a <= b) {
-    if (lane == 0) atomicMin(&c.cnt->key_min, a);
-    if (lane == 1) atomicMax(&c.cnt->key_max, b);
+    if (lane == 0) atomicMin(&c.xc->key_min, a);
+    if (lane == 1) atomicMax(&c.xc->key_max, b);
   }
   if (d <= e) {
-    if (lane == 2) atomicMin(&c.T->pool_key_min, d);
-    if (lane == 3) atomicMax(&c.T->pool_key_max, e);
+    if (lane == 2) atomicMin(&c.xp->pool_key_min, d);
+    if (lane == 3) atomicMax(&c.xp->pool_key_max, e);
   }
 }
 
@@ -386,7 +404,7 @@ __device__ __forceinline__ void push_next(const Ctx &c, double score, uint32_t n
   const uint32_t k32 = (uint32_t)(orderable(score * c.f_next) >> 32);
   c.kmin = min(c.kmin, k32);
   c.kmax = max(c.kmax, k32);
-  const uint32_t i = append_slot(&c.cnt->n_next);
+  const uint32_t i = append_slot(&c.xc->n_next);
   if (i < c.p->cand_cap) {
     Cand v;
     v.score = score;
@@ -402,12 +420,15 @@ __device__ __forceinline__ void push_next(const Ctx &c, double score, uint32_t n
   }
 }
 
+// kHelp (here and down the emission chain): the helper instance, where an
+// open step's pool slots are offset by S->pool_add; elsewhere the offset is 0.
+template <bool kHelp>
 __device__ __forceinline__ void push_pool(const Ctx &c, double score, uint32_t node, uint32_t parent,
                                           uint32_t token) {
   const uint32_t k32 = (uint32_t)(orderable(score * c.f_next) >> 32);
   c.pkmin = min(c.pkmin, k32);
   c.pkmax = max(c.pkmax, k32);
-  const uint32_t i = append_slot(&c.T->pool_end);
+  const uint32_t i = (kHelp ? c.S->pool_add : 0u) + append_slot(&c.xp->pool_end);
   if (i < c.p->pool_cap) {
     Cand v;
     v.score = score;
@@ -461,6 +482,7 @@ __device__ __forceinline__ uint32_t block_exclusive_sum(uint32_t v, LocalState *
 }
 
 // ------------------------------------------------------------ expansion
+template <bool kHelp>
 __device__ void expand_inlink(const Ctx &c) {
   const TrieView &t = c.p->trie;
   const double tt = c.p->token_threshold, st = c.p->sent_threshold;
@@ -500,7 +522,7 @@ __device__ void expand_inlink(const Ctx &c) {
       if (lp <= tt || b.score + lp <= st) continue;
       const double score = b.score + lp;
       if (end) {
-        if (rec_flags(b.dw) & kNodeFlagTerminal) push_pool(c, score, b.node, i, tok);
+        if (rec_flags(b.dw) & kNodeFlagTerminal) push_pool<kHelp>(c, score, b.node, i, tok);
       } else {
         push_next(c, score, b.node, off + 1, i, tok, b.c0, b.dw);
       }
@@ -593,8 +615,10 @@ __device__ __forceinline__ void write_next(const Ctx &c, uint32_t idx, double sc
   }
 }
 
+template <bool kHelp>
 __device__ __forceinline__ void write_pool(const Ctx &c, uint32_t idx, double score, uint32_t node, uint32_t parent,
                                            uint32_t token) {
+  if (kHelp) idx += c.S->pool_add;
   const uint32_t k32 = (uint32_t)(orderable(score * c.f_next) >> 32);
   c.pkmin = min(c.pkmin, k32);
   c.pkmax = max(c.pkmax, k32);
@@ -617,7 +641,7 @@ __device__ __forceinline__ void write_pool(const Ctx &c, uint32_t idx, double sc
 // `visit(k, m)` is called for every pair whose log-prob passes the thresholds.
 // The warp counts its candidates and pool entries first, reserves them with
 // one atomic each, then writes them.
-template <class Pairs>
+template <bool kHelp, class Pairs>
 __device__ __forceinline__ void emit_task(const Ctx &c, double pscore, uint32_t parent_idx, const uint32_t child[4],
                                           const uint4 rec[4], Pairs &&pairs) {
   const double tt = c.p->token_threshold, st = c.p->sent_threshold;
@@ -631,7 +655,7 @@ __device__ __forceinline__ void emit_task(const Ctx &c, double pscore, uint32_t 
     np += pl;
   });
   uint32_t bn, bp;
-  warp_reserve2(&c.cnt->n_next, nn, &c.T->pool_end, np, bn, bp);
+  warp_reserve2(&c.xc->n_next, nn, &c.xp->pool_end, np, bn, bp);
   if (nn + np == 0) return;
   pairs([&](uint32_t k, uint32_t m) {
     const double lp = (double)c.row.lp[m];
@@ -643,7 +667,7 @@ __device__ __forceinline__ void emit_task(const Ctx &c, double pscore, uint32_t 
     classify(r.w >> 24, nx, pl);
     const bool link = (r.w >> 24) & kNodeFlagLink;
     if (nx) write_next(c, bn++, score, child[k], link ? r.y + 1 : r.y, parent_idx, token, r.z, r.w);
-    if (pl) write_pool(c, bp++, score, child[k], parent_idx, token);
+    if (pl) write_pool<kHelp>(c, bp++, score, child[k], parent_idx, token);
   });
 }
 
@@ -669,6 +693,7 @@ __device__ __forceinline__ void row_lower_bound4(const RowView &r, const uint32_
 
 // Lookup tasks (called by all 32 lanes of a warp): a lane's four items issue
 // each round of loads before using any.
+template <bool kHelp>
 __device__ __forceinline__ void task_scan(const Ctx &c, uint32_t c0, uint32_t d, uint32_t first_item, double score,
                                           uint32_t parent_idx) {
   const TrieView &t = c.p->trie;
@@ -689,13 +714,14 @@ __device__ __forceinline__ void task_scan(const Ctx &c, uint32_t c0, uint32_t d,
     const uint32_t i = first_item + 32u * k + lane;
     if (i >= d || mlo[k] >= c.row.K || c.row.id[mlo[k]] != x[k]) mlo[k] = c.row.K;
   }
-  emit_task(c, score, parent_idx, child, rec, [&](auto &&fn) {
+  emit_task<kHelp>(c, score, parent_idx, child, rec, [&](auto &&fn) {
 #pragma unroll
     for (uint32_t k = 0; k < kItemsPerLane; ++k)
       for (uint32_t m = mlo[k]; m < c.row.K && c.row.id[m] == x[k]; ++m) fn(k, m);
   });
 }
 
+template <bool kHelp>
 __device__ __forceinline__ void task_hash(const Ctx &c, uint32_t base, uint32_t lg, uint32_t first_item, double score,
                                           uint32_t parent_idx) {
   const TrieView &t = c.p->trie;
@@ -753,13 +779,14 @@ __device__ __forceinline__ void task_hash(const Ctx &c, uint32_t base, uint32_t 
     }
     if (child[k] != 0) rec[k] = __ldg(t.node + child[k]);
   }
-  emit_task(c, score, parent_idx, child, rec, [&](auto &&fn) {
+  emit_task<kHelp>(c, score, parent_idx, child, rec, [&](auto &&fn) {
 #pragma unroll
     for (uint32_t k = 0; k < kItemsPerLane; ++k)
       if (child[k] != 0) fn(k, first_item + 32u * k + lane);
   });
 }
 
+template <bool kHelp>
 __device__ __forceinline__ void task_bin(const Ctx &c, uint32_t c0, uint32_t d, uint32_t first_item, double score,
                                          uint32_t parent_idx) {
   const TrieView &t = c.p->trie;
@@ -804,7 +831,7 @@ __device__ __forceinline__ void task_bin(const Ctx &c, uint32_t c0, uint32_t d, 
     }
     if (child[k] != 0) rec[k] = __ldg(t.node + child[k]);
   }
-  emit_task(c, score, parent_idx, child, rec, [&](auto &&fn) {
+  emit_task<kHelp>(c, score, parent_idx, child, rec, [&](auto &&fn) {
 #pragma unroll
     for (uint32_t k = 0; k < kItemsPerLane; ++k)
       if (child[k] != 0) fn(k, first_item + 32u * k + lane);
@@ -831,90 +858,188 @@ __device__ __forceinline__ uint32_t task_parent(const BranchTable &bt, uint32_t 
   return lo;
 }
 
-__device__ void expand_branch(const Ctx &c, const BranchTable &bt) {
+// Builds the task table of one chunk of m branching parents starting at
+// c_first (every CTA builds the same one): per parent its child range, mode
+// and first task.  Returns the chunk's task count.
+__device__ uint32_t build_table(const Ctx &c, const BranchTable &bt, uint32_t c_first, uint32_t m) {
   const TrieView &t = c.p->trie;
-  const uint32_t lane = threadIdx.x & 31;
-  const uint32_t n_br = c.S->n_br;
   const uint32_t K = c.row.K;
   const uint32_t beam_cap = c.p->beam_cap;
+  uint32_t my_tasks[kParentChunk / kSearchThreads];
+#pragma unroll
+  for (uint32_t r = 0; r < kParentChunk / kSearchThreads; ++r) {
+    const uint32_t q = threadIdx.x * (kParentChunk / kSearchThreads) + r;
+    my_tasks[r] = 0;
+    if (q >= m) continue;
+    const uint32_t idx = beam_cap - 1 - (c_first + q);
+    const Beam b = ld_beam(c.cur + idx);
+    uint4 info = make_uint4(0, 0, 0, 0);
+    if ((uint64_t)b.node >= t.num_nodes) {
+      atomicOr(c.p->status, kStatusNodeBounds);
+    } else {
+      // The beam carries its node's child range and flags.
+      const uint32_t c0 = b.c0;
+      uint32_t d = b.dw & kFanoutMask;
+      if (d == kFanoutMask) {
+        const uint32_t end = (uint64_t)b.node + 1 < t.num_nodes ? __ldg(t.node + b.node + 1).z
+                                                               : (uint32_t)t.num_nodes;
+        d = end > c0 ? end - c0 : 0;
+      }
+      if ((uint64_t)c0 + d > t.num_nodes) {
+        atomicOr(c.p->status, kStatusNodeBounds);
+        d = 0;
+      }
+      const uint32_t f = rec_flags(b.dw);
+      const uint32_t mode = pick_mode(d, K, f);
+      const uint32_t items = (d == 0) ? 0u : (mode == kModeScan ? d : K);
+      info = make_uint4(c0, d, b.off, mode | ((f >> 3) << 8));
+      my_tasks[r] = (items + kTaskItems - 1) / kTaskItems;
+    }
+    bt.info[q] = info;
+    bt.score[q] = b.score;
+  }
+  uint32_t sum = 0;
+#pragma unroll
+  for (uint32_t r = 0; r < kParentChunk / kSearchThreads; ++r) sum += my_tasks[r];
+  uint32_t pre = block_exclusive_sum(sum, c.S);
+#pragma unroll
+  for (uint32_t r = 0; r < kParentChunk / kSearchThreads; ++r) {
+    const uint32_t q = threadIdx.x * (kParentChunk / kSearchThreads) + r;
+    if (q < m) bt.start[q] = pre;
+    pre += my_tasks[r];
+  }
+  if (threadIdx.x == blockDim.x - 1) c.S->n_tasks = pre;
+  __syncthreads();
+  return c.S->n_tasks;
+}
+
+// One task of the chunk (called by all 32 lanes of a warp).
+template <bool kHelp>
+__device__ __forceinline__ void run_task(const Ctx &c, const BranchTable &bt, uint32_t c_first, uint32_t m,
+                                         uint32_t task) {
+  const uint32_t lo = task_parent(bt, m, task);
+  const uint4 info = bt.info[lo];
+  const double score = bt.score[lo];
+  const uint32_t first_item = (task - bt.start[lo]) * kTaskItems;
+  const uint32_t mode = info.w & 0xFFu;
+  const uint32_t parent_idx = c.p->beam_cap - 1 - (c_first + lo);
+  if (mode == kModeScan) {
+    task_scan<kHelp>(c, info.x, info.y, first_item, score, parent_idx);
+  } else if (mode == kModeHash) {
+    task_hash<kHelp>(c, info.z, info.w >> 8, first_item, score, parent_idx);
+  } else {
+    task_bin<kHelp>(c, info.x, info.y, first_item, score, parent_idx);
+  }
+}
+
+__device__ __forceinline__ uint32_t vld(const uint32_t *p) { return *reinterpret_cast<const volatile uint32_t *>(p); }
+__device__ __forceinline__ unsigned long long vld64(const unsigned long long *p) {
+  return *reinterpret_cast<const volatile unsigned long long *>(p);
+}
+__device__ __forceinline__ void vst(uint32_t *p, uint32_t v) { *reinterpret_cast<volatile uint32_t *>(p) = v; }
+__device__ __forceinline__ void vst64(unsigned long long *p, unsigned long long v) {
+  *reinterpret_cast<volatile unsigned long long *>(p) = v;
+}
+
+// Branching beams of a step, chunk by chunk (kParentChunk parents each).
+// Every warp runs task `wid` first (no wait); the tasks beyond the team's
+// warps are handed out on demand from the team's counter: a warp asks for its
+// next task before it runs the current one, so the round trip overlaps the
+// task, and a warp that drew cheap tasks takes more.  Later chunks (beam
+// widths above 1024) go round-robin.
+// A step opened to helper clusters (c.help, helper instance): all tasks of the
+// first chunk come from the step's claim counter in the HelpState, shared by
+// the leader team's CTAs (which wait until rank 0 has armed the step) and the
+// helpers' (which run only this chunk, started after the step's `go`).  Each
+// warp counts the tasks it ran into `done` (a helper after publishing its key
+// ranges, behind a fence); rank 0 of the leader then waits until every task
+// handed out has finished.  A claim at or beyond the task count ends a warp's
+// share; a helper that started late may have built its table from a later
+// step's beams, so it bounds claims by the count the leader published, once
+// known (before then the step is open and its table is right).
+template <bool kHelp>
+__device__ void expand_branch(const Ctx &c, const BranchTable &bt) {
+  const uint32_t lane = threadIdx.x & 31;
+  const uint32_t n_br = c.S->n_br;
   const uint32_t team_warps = c.cs * kWarps;
   const uint32_t wid = c.rank * kWarps + (threadIdx.x >> 5);
+  const bool helper = c.T == nullptr;
   for (uint32_t c_first = 0; c_first < n_br; c_first += kParentChunk) {
     const uint32_t m = min(kParentChunk, n_br - c_first);
-    uint32_t my_tasks[kParentChunk / kSearchThreads];
-#pragma unroll
-    for (uint32_t r = 0; r < kParentChunk / kSearchThreads; ++r) {
-      const uint32_t q = threadIdx.x * (kParentChunk / kSearchThreads) + r;
-      my_tasks[r] = 0;
-      if (q >= m) continue;
-      const uint32_t idx = beam_cap - 1 - (c_first + q);
-      const Beam b = ld_beam(c.cur + idx);
-      uint4 info = make_uint4(0, 0, 0, 0);
-      if ((uint64_t)b.node >= t.num_nodes) {
-        atomicOr(c.p->status, kStatusNodeBounds);
-      } else {
-        // The beam carries its node's child range and flags.
-        const uint32_t c0 = b.c0;
-        uint32_t d = b.dw & kFanoutMask;
-        if (d == kFanoutMask) {
-          const uint32_t end = (uint64_t)b.node + 1 < t.num_nodes ? __ldg(t.node + b.node + 1).z
-                                                                 : (uint32_t)t.num_nodes;
-          d = end > c0 ? end - c0 : 0;
+    const uint32_t total = build_table(c, bt, c_first, m);
+    const bool claimed = kHelp && c.help && c_first == 0;
+    const uint32_t lim = total;
+    if (kHelp && claimed) {
+      if (threadIdx.x == 0 && !helper) {
+        // Claim only once this CTA sees the step armed (bounded wait).
+        const unsigned long long deadline = global_ns() + kHelpWaitNs;
+        while (vld(help_word(c.help, kHelpArm, c.step)) != c.S->help_epoch) {
+          if (global_ns() > deadline) {
+            atomicOr(c.p->status, kStatusHelp);
+            break;
+          }
+          __nanosleep(32);
         }
-        if ((uint64_t)c0 + d > t.num_nodes) {
-          atomicOr(c.p->status, kStatusNodeBounds);
-          d = 0;
-        }
-        const uint32_t f = rec_flags(b.dw);
-        const uint32_t mode = pick_mode(d, K, f);
-        const uint32_t items = (d == 0) ? 0u : (mode == kModeScan ? d : K);
-        info = make_uint4(c0, d, b.off, mode | ((f >> 3) << 8));
-        my_tasks[r] = (items + kTaskItems - 1) / kTaskItems;
+        __threadfence();
+        if (c.rank == 0) vst(help_word(c.help, kHelpTotal, c.step), total);
       }
-      bt.info[q] = info;
-      bt.score[q] = b.score;
+      __syncthreads();
     }
-    uint32_t sum = 0;
-#pragma unroll
-    for (uint32_t r = 0; r < kParentChunk / kSearchThreads; ++r) sum += my_tasks[r];
-    uint32_t pre = block_exclusive_sum(sum, c.S);
-#pragma unroll
-    for (uint32_t r = 0; r < kParentChunk / kSearchThreads; ++r) {
-      const uint32_t q = threadIdx.x * (kParentChunk / kSearchThreads) + r;
-      if (q < m) bt.start[q] = pre;
-      pre += my_tasks[r];
-    }
-    if (threadIdx.x == blockDim.x - 1) c.S->n_tasks = pre;
-    __syncthreads();
-    const uint32_t total = c.S->n_tasks;
-    // Every warp runs task `wid` first (no wait).  In the first chunk, tasks
-    // beyond the team's warps are handed out on demand from the team's
-    // counter: a warp asks for its next task before it runs the current one,
-    // so the round trip overlaps the task, and a warp that drew cheap tasks
-    // takes more.  Later chunks (beam widths above 1024) go round-robin.
-    const uint32_t n_dyn = (c_first == 0 && total > team_warps) ? total - team_warps : 0u;
+    const uint32_t n_dyn = (!claimed && c_first == 0 && total > team_warps) ? total - team_warps : 0u;
     uint32_t task = wid;
-    while (task < total) {
-      uint32_t nxt = 0xFFFFFFFFu;
-      if (n_dyn && lane == 0) nxt = atomicAdd(&c.cnt->task_next, 1u);
-      const uint32_t lo = task_parent(bt, m, task);
-      const uint4 info = bt.info[lo];
-      const double score = bt.score[lo];
-      const uint32_t first_item = (task - bt.start[lo]) * kTaskItems;
-      const uint32_t mode = info.w & 0xFFu;
-      const uint32_t parent_idx = beam_cap - 1 - (c_first + lo);
-      if (mode == kModeScan) {
-        task_scan(c, info.x, info.y, first_item, score, parent_idx);
-      } else if (mode == kModeHash) {
-        task_hash(c, info.z, info.w >> 8, first_item, score, parent_idx);
-      } else {
-        task_bin(c, info.x, info.y, first_item, score, parent_idx);
+    if (kHelp && claimed) {
+      uint32_t v = 0;
+      if (lane == 0) {
+        v = atomicAdd(help_word(c.help, kHelpClaim, c.step), 1u);
+        if (helper) {
+          const uint32_t pt = vld(help_word(c.help, kHelpTotal, c.step));
+          if (pt != 0xFFFFFFFFu && v >= pt) v = 0xFFFFFFFFu;
+        }
       }
-      if (n_dyn) {
+      task = __shfl_sync(0xFFFFFFFFu, v, 0);
+    }
+    uint32_t mine = 0;
+    while (task < lim) {
+      uint32_t nxt = 0xFFFFFFFFu;
+      if (lane == 0) {
+        if (kHelp && claimed) {
+          nxt = atomicAdd(help_word(c.help, kHelpClaim, c.step), 1u);
+        } else if (n_dyn) {
+          nxt = atomicAdd(&c.xc->task_next, 1u);
+        }
+      }
+      run_task<kHelp>(c, bt, c_first, m, task);
+      ++mine;
+      if (kHelp && claimed) {
+        if (helper && lane == 0) {
+          const uint32_t pt = vld(help_word(c.help, kHelpTotal, c.step));
+          if (pt != 0xFFFFFFFFu && nxt >= pt) nxt = 0xFFFFFFFFu;
+        }
+        task = __shfl_sync(0xFFFFFFFFu, nxt, 0);
+      } else if (n_dyn) {
         const uint32_t v = __shfl_sync(0xFFFFFFFFu, nxt, 0);
         task = v < n_dyn ? team_warps + v : total;
       } else {
         task += team_warps;
+      }
+    }
+    if (kHelp && claimed) {
+      if (helper) {
+        publish_ranges(c);
+        __threadfence();
+        __syncwarp();
+      }
+      if (lane == 0 && mine) atomicAdd(help_word(c.help, kHelpDone, c.step), mine);
+      if (!helper && c.rank == 0 && threadIdx.x == 0) {
+        const unsigned long long deadline = global_ns() + kHelpWaitNs;
+        while (vld(help_word(c.help, kHelpDone, c.step)) < total) {
+          if (global_ns() > deadline) {
+            atomicOr(c.p->status, kStatusHelp);
+            break;
+          }
+          __nanosleep(32);
+        }
+        __threadfence();
       }
     }
     __syncthreads();  // the task table is rebuilt for the next chunk
@@ -1196,6 +1321,7 @@ __device__ __forceinline__ int common_bits(uint32_t lo, uint32_t hi) {
 // back; the capped total keeps the two from overlapping.  The converged
 // threads reserve together: one thread issues the three counter atomics back
 // to back (one round trip) for all of them.
+template <bool kCount>
 __device__ __forceinline__ void take_beam(const Ctx &c, const Cand &v, uint32_t k, Beam *out_beams, Hist *hist) {
   const uint32_t act = __activemask();
   const uint32_t lane = threadIdx.x & 31;
@@ -1203,11 +1329,20 @@ __device__ __forceinline__ void take_beam(const Ctx &c, const Cand &v, uint32_t 
   const uint32_t m_in = __ballot_sync(act, link);
   const uint32_t m_br = act & ~m_in;
   const uint32_t leader = __ffs(act) - 1;
+  uint32_t n_tasks = 0;
+  if (kCount) {
+    // This beam's branch tasks at the next step, as the task table will
+    // count them (an escaped fan-out is large: one task per 128 proposals).
+    const uint32_t d = v.dw & kFanoutMask, K = c.row.K;
+    const uint32_t items = (link || d == 0) ? 0u : (d <= 2u * K + 32u ? d : K);
+    n_tasks = __reduce_add_sync(act, (items + kTaskItems - 1) / kTaskItems);
+  }
   uint32_t b_sel = 0, b_in = 0, b_br = 0;
   if (lane == leader) {
     b_sel = atomicAdd(&c.cnt->n_sel, (uint32_t)__popc(act));
     if (m_in) b_in = atomicAdd(&c.cnt->n_in_new, (uint32_t)__popc(m_in));
     if (m_br) b_br = atomicAdd(&c.cnt->n_br_new, (uint32_t)__popc(m_br));
+    if (n_tasks) atomicAdd(&c.cnt->n_tasks_new, n_tasks);
   }
   b_sel = __shfl_sync(act, b_sel, leader);
   b_in = __shfl_sync(act, b_in, leader);
@@ -1234,7 +1369,9 @@ __device__ __forceinline__ void take_beam(const Ctx &c, const Cand &v, uint32_t 
   hist[idx] = Hist{v.parent, v.token};
 }
 
-// Makes the selected candidates the beams of step t+1.
+// Makes the selected candidates the beams of step t+1 (kCount: and sums their
+// branch tasks for the next step, when c.count_tasks).
+template <bool kCount>
 __device__ void materialize_next(const Ctx &c, uint32_t n, uint32_t k, Beam *out_beams) {
   const uint32_t depth = c.step + 1;
   const double f = c.p->factor[depth];
@@ -1256,7 +1393,7 @@ __device__ void materialize_next(const Ctx &c, uint32_t n, uint32_t k, Beam *out
     team_radix_select(c, k, start, c.S->key_min, c.S->key_max, true, [&](const RadixPass &rp, uint32_t *h) {
       if (have) hist_add(key, rp, h);
     });
-    if (have && is_selected(c, key, &c.cnt->eq_taken)) take_beam(c, v, k, out_beams, hist);
+    if (have && is_selected(c, key, &c.cnt->eq_taken)) take_beam<kCount>(c, v, k, out_beams, hist);
     return;
   }
   const bool all = n <= k;
@@ -1277,7 +1414,7 @@ __device__ void materialize_next(const Ctx &c, uint32_t n, uint32_t k, Beam *out
   for (uint32_t i = c.gtid(); i < n; i += G) {
     const uint4 a = ld_cand_head(next + i);
     if (!all && !is_selected(c, head_key(a, f, depth), &c.cnt->eq_taken)) continue;
-    take_beam(c, cand_from(a, next + i), k, out_beams, hist);
+    take_beam<kCount>(c, cand_from(a, next + i), k, out_beams, hist);
   }
 }
 
@@ -1456,22 +1593,48 @@ __device__ void stage_row(const SearchParams &p, const RowView &row, uint64_t rb
 }
 
 __device__ void reset_counters(StepCounters *s) {
-  s->n_next = 0;
-  s->key_min = 0xFFFFFFFFu;
-  s->key_max = 0;
   s->n_sel = 0;
   s->n_in_new = 0;
   s->n_br_new = 0;
   s->eq_taken = 0;
-  s->task_next = 0;
+  s->n_tasks_new = 0;
+}
+
+__device__ void reset_exp(ExpCounters *x) {
+  x->n_next = 0;
+  x->key_min = 0xFFFFFFFFu;
+  x->key_max = 0;
+  x->task_next = 0;
+}
+
+__device__ void reset_pool(PoolCounters *x) {
+  x->pool_end = 0;
+  x->pool_key_min = 0xFFFFFFFFu;
+  x->pool_key_max = 0;
 }
 
 // One request, searched by the whole team.  Cluster barriers per step: one
 // after expansion, one per radix pass of the selection, one after the next
 // beams are written (plus the passes of a pool trim when the next step could
 // overflow the pool).
+// Splits the dynamic shared memory into the staged row and the task table.
+__device__ __forceinline__ void carve(uint8_t *dyn, uint32_t K, RowView &row, BranchTable &bt) {
+  row.id = reinterpret_cast<uint32_t *>(dyn);
+  row.lp = reinterpret_cast<float *>(dyn + sizeof(uint32_t) * K);
+  row.orig = reinterpret_cast<uint32_t *>(dyn + 2 * sizeof(uint32_t) * K);
+  row.K = K;
+  uint8_t *tb = dyn + ((12u * K + 15u) & ~15u);
+  bt.info = reinterpret_cast<uint4 *>(tb);
+  bt.score = reinterpret_cast<double *>(tb + sizeof(uint4) * kParentChunk);
+  bt.start = reinterpret_cast<uint32_t *>(tb + (sizeof(uint4) + sizeof(double)) * kParentChunk);
+}
+
+// `epoch` names this request of this launch; `kord` is the request's
+// ordinal among its slot's requests in this launch (helper bookkeeping).
+template <bool kHelp>
 __device__ void search_request(const SearchParams &p, uint32_t req, const SlotView &slot, TeamState *T,
-                               LocalState *S, uint32_t rank, uint32_t cs, uint8_t *dyn) {
+                               LocalState *S, uint32_t rank, uint32_t cs, uint8_t *dyn, uint32_t epoch,
+                               uint32_t kord) {
   const ReqMeta meta = p.meta[req];
   const uint32_t L = meta.L, K = meta.K;
   const uint32_t *beams = p.beams + meta.beams_off;
@@ -1515,29 +1678,41 @@ __device__ void search_request(const SearchParams &p, uint32_t req, const SlotVi
     slot.beams[0][beam_cap - 1] = root;
     reset_counters(&T->cnt[0]);
     reset_counters(&T->cnt[1]);
-    T->pool_end = 0;
-    T->pool_key_min = 0xFFFFFFFFu;
-    T->pool_key_max = 0;
+    reset_exp(&T->xc[0]);
+    reset_exp(&T->xc[1]);
+    reset_pool(&T->pool);
     T->n_compact = 0;
     T->eq_taken_trim = 0;
     T->removed = 0;
   }
+  // Helper clusters: the counters they share live in the slot's HelpState.
+  // Its per-step words are re-armed only when every helper of this slot's
+  // previous request in this launch has left that request (bounded wait; a
+  // launch's first request has none, and every earlier launch has ended).
+  // The HelpState's counters are clear between open steps (set so at
+  // allocation, cleared by the leader after each open step); a step's claim,
+  // done and total words are re-armed when the step opens.
+  HelpState *const H = (kHelp && p.helpers && slot.help) ? slot.help : nullptr;
+  if (H && leader && kord > 0) {
+    __threadfence();
+    const uint32_t q = (kord & 1u) ^ 1u;
+    const unsigned long long deadline = global_ns() + kHelpWaitNs;
+    while (vld(&H->left[q]) != vld(&H->joined[q])) {
+      if (global_ns() > deadline) {
+        atomicOr(p.status, kStatusHelp);
+        break;
+      }
+      __nanosleep(32);
+    }
+  }
+  if (threadIdx.x == 0) S->help_epoch = epoch;
   if (threadIdx.x == 0) S->pass = 0;
   // Both histogram buffers start clear; afterwards each pass clears the
   // buffer of the pass after it (team_radix_select).
   for (uint32_t b = threadIdx.x; b < 2 * kRadixBins; b += blockDim.x) (&S->hist[0][0])[b] = 0;
   RowView row;
-  row.id = reinterpret_cast<uint32_t *>(dyn);
-  row.lp = reinterpret_cast<float *>(dyn + sizeof(uint32_t) * K);
-  row.orig = reinterpret_cast<uint32_t *>(dyn + 2 * sizeof(uint32_t) * K);
-  row.K = K;
   BranchTable bt;
-  {
-    uint8_t *tb = dyn + ((12u * K + 15u) & ~15u);
-    bt.info = reinterpret_cast<uint4 *>(tb);
-    bt.score = reinterpret_cast<double *>(tb + sizeof(uint4) * kParentChunk);
-    bt.start = reinterpret_cast<uint32_t *>(tb + (sizeof(uint4) + sizeof(double)) * kParentChunk);
-  }
+  carve(dyn, K, row, bt);
   team_sync(cs);
 
   Ctx c;
@@ -1548,6 +1723,9 @@ __device__ void search_request(const SearchParams &p, uint32_t req, const SlotVi
   c.row = row;
   c.rank = rank;
   c.cs = cs;
+  c.help = nullptr;
+  c.xp = &T->pool;
+  if (threadIdx.x == 0) S->pool_add = 0;
   bool trimmed = false;  // the previous step left its pool survivors in pool_tmp
   uint32_t prev_want = 0;
   for (uint32_t t = 0; t < L; ++t) {
@@ -1556,6 +1734,8 @@ __device__ void search_request(const SearchParams &p, uint32_t req, const SlotVi
     if (leader) t0 = global_ns();
     c.step = t;
     c.cnt = &T->cnt[par];
+    c.xc = &T->xc[par];
+    c.help = nullptr;
     if (threadIdx.x == 0) {
       if (t == 0) {
         S->n_in = 0;
@@ -1573,10 +1753,40 @@ __device__ void search_request(const SearchParams &p, uint32_t req, const SlotVi
         }
         S->n_in = min(n_in, beam_cap);
         S->n_br = min(n_br, beam_cap - S->n_in);
+        S->est_tasks = pc->n_tasks_new;
       }
-      S->pushes = (unsigned long long)T->pool_end + T->removed;
+      S->pool_base = vld(&c.xp->pool_end);
+      S->pushes = (unsigned long long)S->pool_base + T->removed;
+      // A step whose branching beams bring many tasks (summed by the last
+      // selection) is opened to the helpers; every CTA decides alike and
+      // rank 0 publishes it.  Its counters move to the HelpState: pool
+      // entries go after the pool's end at the step's start (pool_base), the
+      // HelpState's pool counter is zero between open steps, and the leader
+      // folds it back after the step's expansion barrier.
+      const bool go_on = !(S->stop || S->n_in + S->n_br == 0 || (p.early_exit && S->pushes >= final_beam));
+      S->help_open = (H && go_on && t > 0 && S->est_tasks >= kHelpMinTasks && t < H->steps) ? 1u : 0u;
+      S->pool_add = S->help_open ? S->pool_base : 0u;
+      if (S->help_open && rank == 0) {
+        // Re-arm the step's words, the arm word last: the team's CTAs claim
+        // only once they see it, and by then the other words are visible;
+        // helpers see them through the fence before `go`.
+        *help_word(H, kHelpClaim, t) = 0;
+        *help_word(H, kHelpDone, t) = 0;
+        *help_word(H, kHelpTotal, t) = 0xFFFFFFFFu;
+        *help_word(H, kHelpNbr, t) = S->n_br;
+        H->pool.base = S->pool_base;
+        __threadfence();
+        vst(help_word(H, kHelpArm, t), epoch);
+        __threadfence();
+        vst64(&H->go, ((unsigned long long)epoch << 32) | t);
+      }
     }
     __syncthreads();
+    if (S->help_open) {
+      c.help = H;
+      c.xc = &H->xc[par];
+      c.xp = &H->pool;
+    }
     if (trimmed) {
       // Survivors of the previous step's trim go back to the pool's front;
       // this step appends behind them, and the pool is next read after the
@@ -1594,31 +1804,51 @@ __device__ void search_request(const SearchParams &p, uint32_t req, const SlotVi
     c.f_next = p.factor[t + 1];
     c.kmin = c.pkmin = 0xFFFFFFFFu;
     c.kmax = c.pkmax = 0;
-    expand_inlink(c);
-    expand_branch(c, bt);
+    expand_inlink<kHelp>(c);
+    expand_branch<kHelp>(c, bt);
     publish_ranges(c);
     team_sync(cs);
     unsigned long long t2 = 0;
     if (leader) t2 = global_ns();
 
     if (threadIdx.x == 0) {
-      S->n_next = min(c.cnt->n_next, (uint32_t)p.cand_cap);
-      S->pool_end = min(T->pool_end, (uint32_t)p.pool_cap);
-      S->key_min = c.cnt->key_min;
-      S->key_max = c.cnt->key_max;
-      S->pool_key_min = T->pool_key_min;
-      S->pool_key_max = T->pool_key_max;
+      S->n_next = min(vld(&c.xc->n_next), (uint32_t)p.cand_cap);
+      S->key_min = vld(&c.xc->key_min);
+      S->key_max = vld(&c.xc->key_max);
+      if (c.help) {
+        // An open step's pool entries were counted in the HelpState.
+        S->pool_end = min(S->pool_base + vld(&H->pool.pool_end), (uint32_t)p.pool_cap);
+        S->pool_key_min = min(vld(&T->pool.pool_key_min), vld(&H->pool.pool_key_min));
+        S->pool_key_max = max(vld(&T->pool.pool_key_max), vld(&H->pool.pool_key_max));
+      } else {
+        S->pool_end = min(vld(&c.xp->pool_end), (uint32_t)p.pool_cap);
+        S->pool_key_min = vld(&c.xp->pool_key_min);
+        S->pool_key_max = vld(&c.xp->pool_key_max);
+      }
     }
     __syncthreads();
     // Every CTA has read step t-1's counters and the last trim's count
     // (before the barrier above).
     if (leader) {
       reset_counters(&T->cnt[par ^ 1u]);
+      reset_exp(&T->xc[par ^ 1u]);
+      if (c.help) {
+        // Every CTA has read the open step's counters (above): fold the
+        // pool's into the team's and clear the HelpState's for the next open
+        // step.
+        T->pool.pool_end = S->pool_end;
+        T->pool.pool_key_min = S->pool_key_min;
+        T->pool.pool_key_max = S->pool_key_max;
+        reset_pool(&H->pool);
+        reset_exp(&H->xc[par]);
+      }
       T->n_compact = 0;
       T->eq_taken_trim = 0;
     }
+    c.xp = &T->pool;
+    if (threadIdx.x == 0) S->pool_add = 0;
     const uint32_t n_next = S->n_next, pool_end = S->pool_end;
-    materialize_next(c, n_next, beams[t], slot.beams[par ^ 1u]);
+    materialize_next<kHelp>(c, n_next, beams[t], slot.beams[par ^ 1u]);
     prev_want = min(n_next, beams[t]);
     // Trim the pool only when the next step's appends (at most K per beam)
     // could overflow it.
@@ -1627,7 +1857,7 @@ __device__ void search_request(const SearchParams &p, uint32_t req, const SlotVi
       trim_pool(c, pool_end, final_beam);
       if (leader) {
         T->removed += pool_end - final_beam;
-        T->pool_end = final_beam;
+        c.xp->pool_end = final_beam;
       }
       trimmed = true;
     }
@@ -1642,11 +1872,13 @@ __device__ void search_request(const SearchParams &p, uint32_t req, const SlotVi
   // The pool survivors copied back at the last step start must land before
   // the final trim reads the pool.
   team_sync(cs);
+  // The helpers are done with this request.
+  if (H && leader) vst64(&H->go, ((unsigned long long)epoch << 32) | kHelpStop);
   const unsigned long long t4 = leader ? global_ns() : 0ull;
   if (threadIdx.x == 0) {
-    S->pool_end = min(T->pool_end, (uint32_t)p.pool_cap);
-    S->pool_key_min = T->pool_key_min;
-    S->pool_key_max = T->pool_key_max;
+    S->pool_end = min(vld(&c.xp->pool_end), (uint32_t)p.pool_cap);
+    S->pool_key_min = vld(&c.xp->pool_key_min);
+    S->pool_key_max = vld(&c.xp->pool_key_max);
   }
   __syncthreads();
   if (leader) {
@@ -1684,12 +1916,99 @@ __device__ void search_request(const SearchParams &p, uint32_t req, const SlotVi
   }
 }
 
+// A helper CTA's share of a request: for every step the leader opens (its
+// `go` word), stage the step's row, build the same task table from the
+// step's beams and run tasks from the step's claim counter; then publish the
+// candidates' key ranges and count the tasks done (after a fence, so the
+// leader sees the candidates once it sees the count).  Waits are bounded: a
+// helper whose leader never opens a step, or is not resident, gives up and
+// the leader runs every task itself.  It registers in joined[kpar] before
+// reading `go` and in left[kpar] when it leaves.
+__device__ void help_request(const SearchParams &p, uint32_t req, const SlotView &slot, LocalState *S,
+                             uint8_t *dyn, uint32_t epoch, uint32_t kpar) {
+  HelpState *const H = slot.help;
+  const ReqMeta meta = p.meta[req];
+  const uint32_t L = meta.L, K = meta.K;
+  if (threadIdx.x == 0) {
+    atomicAdd(&H->joined[kpar], 1u);
+    __threadfence();
+  }
+  RowView row;
+  BranchTable bt;
+  carve(dyn, K, row, bt);
+  Ctx c;
+  c.p = &p;
+  c.slot = slot;
+  c.T = nullptr;
+  c.cnt = nullptr;
+  c.S = S;
+  c.row = row;
+  c.rank = 0;
+  c.cs = 1;
+  c.help = H;
+  c.xp = &H->pool;
+  if (threadIdx.x == 0) S->help_epoch = epoch;
+  uint32_t t_next = 0;
+  for (;;) {
+    if (threadIdx.x == 0) {
+      uint32_t got = kHelpStop;
+      const unsigned long long deadline = global_ns() + kHelpWaitNs;
+      // Polls back off (up to ~1 us between them): idle helpers must not
+      // crowd the L2 slice that holds `go` while their leader works.
+      uint32_t nap = 32;
+      while (global_ns() < deadline) {
+        const unsigned long long g = vld64(&H->go);
+        const uint32_t ge = (uint32_t)(g >> 32);
+        if (ge == epoch) {
+          const uint32_t st = (uint32_t)g;
+          if (st == kHelpStop) break;
+          if (st >= t_next) {
+            got = st;
+            break;
+          }
+        } else if ((ge >> 16) == (epoch >> 16) && (ge & 0xFFFFu) > (epoch & 0xFFFFu)) {
+          break;  // the leader has moved on to a later request of this launch
+        }
+        __nanosleep(nap);
+        nap = min(2 * nap, kHelpMaxSleepNs);
+      }
+      __threadfence();
+      S->help_step = got;
+    }
+    __syncthreads();
+    const uint32_t t = S->help_step;
+    if (t == kHelpStop || t >= L || t >= H->steps) break;
+    t_next = t + 1;
+    const uint32_t par = t & 1u;
+    c.step = t;
+    c.cur = slot.beams[par];
+    c.f_next = p.factor[t + 1];
+    c.xc = &H->xc[par];
+    c.kmin = c.pkmin = 0xFFFFFFFFu;
+    c.kmax = c.pkmax = 0;
+    stage_row(p, row, meta.rows_off + (uint64_t)t * K, reinterpret_cast<uint64_t *>(bt.info));
+    if (threadIdx.x == 0) {
+      S->n_br = min(kParentChunk, min(vld(help_word(H, kHelpNbr, t)), p.beam_cap));
+      S->pool_add = vld(&H->pool.base);
+    }
+    __syncthreads();
+    expand_branch<true>(c, bt);  // the first chunk only, from the step's claim counter
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(&H->left[kpar], 1u);
+  }
+}
+
 // Two instances: one CTA per SM with up to 128 registers per thread (all
 // launches with teams of 2-16 CTAs, and batches the SMs can hold one request
 // each), and two CTAs per SM at 64 registers per thread (batches larger than
 // the SM count, where twice the requests in flight hide more latency than the
 // spills cost).
-template <int kMinBlocks>
+// kHelp: the instance that runs launches with helper clusters (the one-CTA
+// instance only); the other instances compile none of that code.
+template <int kMinBlocks, bool kHelp>
 __global__ void __launch_bounds__(kSearchThreads, kMinBlocks) tbs_search_kernel(const SearchParams p) {
   extern __shared__ __align__(16) uint8_t dyn[];
   __shared__ TeamState team_state;
@@ -1698,11 +2017,25 @@ __global__ void __launch_bounds__(kSearchThreads, kMinBlocks) tbs_search_kernel(
   const uint32_t cs = cluster.num_blocks();
   const uint32_t rank = cluster.block_rank();
   TeamState *T = cluster.map_shared_rank(&team_state, 0);
-  const uint32_t team = blockIdx.x / cs, n_teams = gridDim.x / cs;
-  const SlotView slot = p.slots[team];
-  for (uint32_t req = team; req < p.n_req; req += n_teams) {
-    search_request(p, req, slot, T, &local_state, rank, cs, dyn);
-    team_sync(cs);  // rank 0's state is reused by the next request
+  // Clusters come in groups of 1 + helpers: the first of a group leads its
+  // slot's requests, the others help with their expansion.
+  const uint32_t per = p.helpers + 1;
+  const uint32_t team = blockIdx.x / cs, n_groups = (gridDim.x / cs) / per;
+  const uint32_t group = team / per, role = team % per;
+  const SlotView slot = p.slots[group];
+  if (role != 0 && (!kHelp || slot.help == nullptr)) return;
+  uint32_t k = 0;
+  for (uint32_t req = group; req < p.n_req; req += n_groups, ++k) {
+    const uint32_t epoch = (p.launch_seq << 16) | (req & 0xFFFFu);
+    if (role == 0) {
+      search_request<kHelp>(p, req, slot, T, &local_state, rank, cs, dyn, epoch, k);
+      // Every path out of the request ends its helpers' wait.
+      if (kHelp && p.helpers && slot.help && rank == 0 && threadIdx.x == 0)
+        vst64(&slot.help->go, ((unsigned long long)epoch << 32) | kHelpStop);
+      team_sync(cs);  // rank 0's state is reused by the next request
+    } else if (kHelp) {
+      help_request(p, req, slot, &local_state, dyn, epoch, k & 1u);
+    }
   }
 }
 
@@ -1929,17 +2262,18 @@ size_t search_smem_bytes(uint32_t max_topk, uint32_t max_final_beam) {
   return std::max<size_t>(std::max(row, sort), 16);
 }
 
-template <int kMinBlocks>
+template <int kMinBlocks, bool kHelp>
 static int raise_smem(size_t search_smem) {
   cudaFuncAttributes a;
-  CUDA_TRY(cudaFuncGetAttributes(&a, tbs_search_kernel<kMinBlocks>));
+  CUDA_TRY(cudaFuncGetAttributes(&a, tbs_search_kernel<kMinBlocks, kHelp>));
   if ((size_t)a.maxDynamicSharedSizeBytes < search_smem)
-    CUDA_TRY(cudaFuncSetAttribute(tbs_search_kernel<kMinBlocks>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)search_smem));
-  CUDA_TRY(cudaFuncSetAttribute(tbs_search_kernel<kMinBlocks>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    CUDA_TRY(cudaFuncSetAttribute(tbs_search_kernel<kMinBlocks, kHelp>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)search_smem));
+  CUDA_TRY(cudaFuncSetAttribute(tbs_search_kernel<kMinBlocks, kHelp>,
+                                cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
   int per_sm = 0;
-  CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tbs_search_kernel<kMinBlocks>, kSearchThreads,
-                                                         search_smem));
+  CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tbs_search_kernel<kMinBlocks, kHelp>,
+                                                         kSearchThreads, search_smem));
   return per_sm;
 }
 
@@ -1980,7 +2314,8 @@ static int sm_count() {
 }
 
 int ensure_search_smem(size_t search_smem) {
-  const int one = raise_smem<1>(search_smem), two = raise_smem<2>(search_smem);
+  const int one = raise_smem<1, false>(search_smem), two = raise_smem<2, false>(search_smem);
+  raise_smem<1, true>(search_smem);
   return std::max(std::max(one, two), 1) * sm_count();
 }
 
@@ -2006,7 +2341,7 @@ int max_search_clusters(int cluster_size, size_t smem_bytes) {
   cfg.attrs = &attr;
   cfg.numAttrs = 1;
   int n = 0;
-  CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, (void *)tbs_search_kernel<1>, &cfg));
+  CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, (void *)tbs_search_kernel<1, false>, &cfg));
   std::lock_guard<std::mutex> lock(pc.mu);
   pc.clusters[key] = n;
   return n;
@@ -2050,7 +2385,7 @@ SearchLaunch plan_search(uint32_t n, size_t smem_bytes) {
       if (it != pc.dense_per_sm.end()) per_sm = it->second;
     }
     if (per_sm < 0) {
-      CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tbs_search_kernel<2>, kSearchThreads,
+      CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tbs_search_kernel<2, false>, kSearchThreads,
                                                              smem_bytes));
       std::lock_guard<std::mutex> lock(pc.mu);
       pc.dense_per_sm[{dev, smem_bytes}] = per_sm;
@@ -2101,6 +2436,23 @@ size_t reserve_l2_persisting(int device) {
   return w.persist;
 }
 
+int search_grid(SearchParams &p, uint32_t n, uint32_t n_slots, const SearchLaunch &l, bool can_help) {
+  static std::atomic<uint32_t> seq{1};  // epochs are never 0, the words' value at allocation
+  const uint32_t teams = (uint32_t)std::max(l.max_teams, 1);
+  const uint32_t groups = std::max<uint32_t>(1u, std::min(std::min(n, n_slots), teams));
+  uint32_t helpers = 0;
+  if (can_help && !l.dense && n < 65536u) {
+    helpers = std::min<uint32_t>(kMaxHelpers, teams / groups - 1u);
+    if (const char *e = getenv("FT_HELPERS")) helpers = std::min<uint32_t>(helpers, (uint32_t)std::max(atoi(e), 0));
+  }
+  p.n_groups = groups;
+  p.helpers = helpers;
+  uint32_t ls = seq.fetch_add(1u) & 0xFFFFu;
+  if (ls == 0) ls = seq.fetch_add(1u) & 0xFFFFu;
+  p.launch_seq = ls;
+  return (int)(groups * (helpers + 1u));
+}
+
 void launch_search(const SearchParams &p, size_t smem_bytes, int grid, cudaStream_t stream, const SearchLaunch &l) {
   if (p.n_req == 0) return;
   cudaLaunchConfig_t cfg = {};
@@ -2133,9 +2485,11 @@ void launch_search(const SearchParams &p, size_t smem_bytes, int grid, cudaStrea
     }
   }
   if (l.dense) {
-    CUDA_TRY(cudaLaunchKernelEx(&cfg, tbs_search_kernel<2>, p));
+    CUDA_TRY(cudaLaunchKernelEx(&cfg, tbs_search_kernel<2, false>, p));
+  } else if (p.helpers) {
+    CUDA_TRY(cudaLaunchKernelEx(&cfg, tbs_search_kernel<1, true>, p));
   } else {
-    CUDA_TRY(cudaLaunchKernelEx(&cfg, tbs_search_kernel<1>, p));
+    CUDA_TRY(cudaLaunchKernelEx(&cfg, tbs_search_kernel<1, false>, p));
   }
 }
 

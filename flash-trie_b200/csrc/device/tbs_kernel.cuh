@@ -85,6 +85,65 @@ constexpr uint32_t kParentChunk = 1024;
 // Items (children or proposals) per expansion task: four per lane.
 constexpr uint32_t kTaskItems = 128;
 
+// State a request's leader team shares with its helper CTAs (global memory,
+// one per slot).  `go` = (epoch << 32) | step: the step the leader opened for
+// helpers, or kHelpStop when the request is over; the epoch names the launch
+// and request, so a value left by an earlier request or launch is never taken
+// for the current one.  The counters are the ones every expanding CTA appends
+// to, by step parity, and the result pool's; in a request without helpers the
+// same counters live in the leader team's shared memory.
+// Counters every CTA that expands a step appends to (one set per step
+// parity), and the result pool's.
+struct ExpCounters {
+  uint32_t n_next;     // candidates appended
+  uint32_t key_min;    // range of the top 32 bits of the candidates' first key word
+  uint32_t key_max;
+  uint32_t task_next;  // branch tasks handed out on demand
+};
+struct PoolCounters {
+  uint32_t pool_end;      // pool entries (append counter)
+  uint32_t pool_key_min;  // range of the top 32 bits of the pool entries' first key word
+  uint32_t pool_key_max;
+  uint32_t base;          // HelpState copy: where an open step's appends start in the pool
+};
+
+// joined[q] / left[q] count helper CTAs that entered / left requests whose
+// ordinal in the slot has parity q: the leader re-arms the per-step counters
+// for a request only when every helper of the request before it has left.
+// The per-step arrays follow the struct (help_word()), `steps` long each.
+struct alignas(16) HelpState {
+  unsigned long long go;
+  uint32_t joined[2], left[2];
+  uint32_t steps, pad0, pad1, pad2;
+  ExpCounters xc[2];
+  PoolCounters pool;
+};
+// Per step t (arrays after the struct, help_words()): claim = branch tasks
+// handed out; done = tasks finished; total = the step's task count
+// (0xFFFFFFFF until the leader has built its table); nbr = branching beams of
+// the step; arm = the epoch of the request that last opened the step (the
+// leader writes it after the other words; its CTAs claim only once they see
+// it, helpers only after `go`).
+constexpr uint32_t kHelpClaim = 0, kHelpDone = 1, kHelpTotal = 2, kHelpNbr = 3, kHelpArm = 4;
+__host__ __device__ inline uint32_t *help_word(HelpState *h, uint32_t which, uint32_t t) {
+  return reinterpret_cast<uint32_t *>(h + 1) + (size_t)which * h->steps + t;
+}
+__host__ __device__ inline size_t help_state_bytes(uint64_t steps) {
+  return (sizeof(HelpState) + 5 * 4 * steps + 15) & ~size_t(15);
+}
+constexpr uint32_t kHelpStop = 0xFFFFFFFFu;
+// Most helper clusters one request gets.
+constexpr uint32_t kMaxHelpers = 8;
+// Helper clusters pay off only where a step can hold many branch tasks (a
+// step is opened to them at 1024 tasks, one task per 128 proposals of a
+// large node): rows of at least kHelpMinTopk proposals and beams of at least
+// kHelpMinBeam.  Elsewhere the kernel instance without helper code runs.
+constexpr uint32_t kHelpMinTopk = 512;
+constexpr uint32_t kHelpMinBeam = 256;
+inline bool helpers_pay(uint32_t topk, uint32_t max_beam) {
+  return topk >= kHelpMinTopk && max_beam >= kHelpMinBeam;
+}
+
 // Device workspace of one search slot (one in-flight request).
 //   pool_cap = beam_cap + 2 * beam_cap * max_topk: a step appends at most
 //   (its beams) * K pool entries, so the pool is trimmed to the final beam
@@ -95,6 +154,7 @@ struct SlotView {
   Cand *pool_tmp;    // [beam_cap]: survivors of a pool trim
   Beam *beams[2];    // [beam_cap] each; in-link beams from the front, branching from the back
   Hist *hist;        // [(max_outpos + 1) * beam_cap]
+  HelpState *help;   // helper state and its per-step arrays, or null (no helpers)
 };
 
 struct SearchParams {
@@ -111,6 +171,12 @@ struct SearchParams {
   uint32_t beam_cap;
   uint32_t n_req;
   uint32_t n_slots;
+  // Requests in flight at once (one slot each) and helper clusters per
+  // request: cluster g of the grid serves slot g / (helpers + 1), as its
+  // leader when g % (helpers + 1) == 0.  helpers = 0: every cluster leads.
+  uint32_t n_groups;
+  uint32_t helpers;
+  uint32_t launch_seq;  // distinct per launch (helper epochs)
   // search parameters
   double token_threshold;
   double sent_threshold;
@@ -136,6 +202,7 @@ constexpr uint32_t kStatusTailBounds = 4u;
 constexpr uint32_t kStatusNodeBounds = 8u;
 constexpr uint32_t kStatusBadRequest = 16u;
 constexpr uint32_t kStatusSelection = 32u;  // a selection did not select exactly k
+constexpr uint32_t kStatusHelp = 64u;       // a bounded wait on helper clusters ran out
 
 // Shared-memory bytes the search kernel needs for a given max K / max final beam.
 size_t search_smem_bytes(uint32_t max_topk, uint32_t max_final_beam);
@@ -149,6 +216,13 @@ struct SearchLaunch {
   int max_teams;
   int dense;
 };
+
+// Teams (clusters) to launch for n requests on `n_slots` slots and helper
+// clusters per request: when fewer requests than resident teams are in
+// flight, each request's leader team gets up to kMaxHelpers helper clusters
+// (only with helper state in the workspace: `can_help`).  Fills
+// p.n_groups / p.helpers and returns the number of teams.
+int search_grid(SearchParams &p, uint32_t n, uint32_t n_slots, const SearchLaunch &l, bool can_help);
 
 // Team size for a batch of n requests: the largest power of two <= 16 with
 // n teams fitting on the device.

@@ -55,6 +55,16 @@ Engine::Engine(std::shared_ptr<DeviceTrie> trie, const EngineLimits &lim) : trie
       slots[s].beams[0] = (Beam *)dalloc(sizeof(Beam) * B);
       slots[s].beams[1] = (Beam *)dalloc(sizeof(Beam) * B);
       slots[s].hist = (Hist *)dalloc(sizeof(Hist) * (L + 1) * B);
+      // Helper state: zeroed (no epoch, no helper inside), then its step count.
+      const size_t hb = help_state_bytes(L);
+      slots[s].help = (HelpState *)dalloc(hb);
+      CUDA_TRY(cudaMemset(slots[s].help, 0, hb));
+      HelpState hs;
+      std::memset(&hs, 0, sizeof(hs));
+      hs.steps = (uint32_t)L;
+      for (int q = 0; q < 2; ++q) hs.xc[q].key_min = 0xFFFFFFFFu;  // clear: empty key ranges
+      hs.pool.pool_key_min = 0xFFFFFFFFu;
+      CUDA_TRY(cudaMemcpy(slots[s].help, &hs, sizeof(hs), cudaMemcpyHostToDevice));
     }
     d_slots_ = (SlotView *)dalloc(sizeof(SlotView) * n_slots_);
     CUDA_TRY(cudaMemcpy(d_slots_, slots.data(), sizeof(SlotView) * n_slots_, cudaMemcpyHostToDevice));
@@ -138,10 +148,11 @@ void Engine::search_host(const ft_request *reqs, uint32_t n, const ft_search_par
   if (n > lim_.max_batch)
     throw InvalidArgument("bs_tbs_gpu: batch_size " + std::to_string(n) + " exceeds max_batch_size = " +
                           std::to_string(lim_.max_batch));
-  uint32_t max_L = 0, max_K = 1, cap = 1;
+  uint32_t max_L = 0, max_K = 1, cap = 1, max_beam = 0;
   uint64_t sum_L = 0, sum_LK = 0;
   for (uint32_t i = 0; i < n; ++i) {
     validate_request(reqs[i]);
+    for (uint32_t t = 0; t < reqs[i].num_outpos; ++t) max_beam = std::max(max_beam, reqs[i].beams[t]);
     if (out[i].capacity < reqs[i].beams[reqs[i].num_outpos - 1] || out[i].stride < reqs[i].num_outpos)
       throw InvalidArgument("tbs: result buffer too small");
     max_L = std::max(max_L, reqs[i].num_outpos);
@@ -220,7 +231,7 @@ void Engine::search_host(const ft_request *reqs, uint32_t n, const ft_search_par
   sp.tok_total = reinterpret_cast<uint64_t *>(d_out + 8);
   sp.out_tok_base = reinterpret_cast<uint64_t *>(d_out + q_base);
   const SearchLaunch plan = plan_search(n, smem_);
-  const int grid = (int)std::min<uint32_t>(std::min<uint32_t>(n, n_slots_), (uint32_t)plan.max_teams);
+  const int grid = search_grid(sp, n, n_slots_, plan, helpers_pay(max_K, max_beam));
   launch_search(sp, smem_, grid, stream_, plan);
   // Small batches: everything in one copy.  Large ones: the headers first,
   // then only the tokens produced.
@@ -331,7 +342,9 @@ void Engine::search_device(const ft_device_batch &b, const ft_search_params &prm
   sp.out_phase_ms = nullptr;
   sp.status = d_status_dev_;
   const SearchLaunch plan = plan_search(b.n, smem_);
-  const int grid = (int)std::min<uint32_t>(std::min<uint32_t>(b.n, n_slots_), (uint32_t)plan.max_teams);
+  // The beam widths are in device memory: the output capacity (at least the
+  // final width) stands in for them.
+  const int grid = search_grid(sp, b.n, n_slots_, plan, helpers_pay(b.topk, b.out_capacity));
   launch_search(sp, smem_, grid, stream, plan);
 }
 
