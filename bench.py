@@ -84,6 +84,10 @@ def parse():
     ap.add_argument("--trie-dir", default="/tmp")
     ap.add_argument("--nonempty-only", action="store_true",
                     help="reference-gpu: search only requests the oracle gives at least one result")
+    ap.add_argument("--with-ref-gpu", action="store_true",
+                    help="add the reference kernel's line (reference_gpu) also with --no-extras")
+    ap.add_argument("--no-north-star", action="store_true",
+                    help="skip the north_star field (config 4, 800M keys, measured in a child process)")
     return ap.parse_args()
 
 
@@ -601,6 +605,13 @@ def run_b200(args, cfg):
     else:
         barrier = lambda: None  # noqa: E731
 
+    # The north star's point runs first, in a child process, while this
+    # process holds no device memory (its key generation and device image
+    # need most of the GPU).
+    north_star = None
+    if world == 1 and args.config == 3 and not (args.no_extras or args.no_north_star):
+        north_star = north_star_subprocess(args)
+
     t_setup = time.time()
     meta = trie_meta(args, cfg)
     if meta is None:
@@ -769,8 +780,10 @@ def run_b200(args, cfg):
                    "sample": "%d request(s) of config %d, %.1f s, reference tbs(use_gpu=False), one process "
                              "pinned to one core" % (cpu_n, args.config, cpu_wall),
                    "ms_per_request": float(np.mean(cpu_ms))}
-        if world == 1 and ref_built() and not args.no_extras:
+        if world == 1 and ref_built() and (args.with_ref_gpu or not args.no_extras):
             extras["reference_gpu"] = reference_gpu_subprocess(args, cfg)
+        if north_star is not None:
+            extras["north_star"] = north_star
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
@@ -824,6 +837,39 @@ def reference_gpu_subprocess(args, cfg):
         return {"unavailable": "reference-gpu exited %d: %s" % (r.returncode, r.stderr[-300:])}
     except subprocess.TimeoutExpired:
         return {"unavailable": "reference-gpu took more than 900 s"}
+
+
+def north_star_subprocess(args):
+    """The north star's own point, beam 1000 at batch 1 on config 4's trie
+    (800M keys), in a child process: its latency, oracle parity and the
+    reference kernel on the same requests.  The child builds (or reuses) the
+    trie file in the same directory."""
+    cmd = [sys.executable, os.path.abspath(__file__), "--config", "4", "--batch", "1", "--steps", "20", "--warmup",
+           "5", "--no-extras", "--cpu-budget", "0", "--trie-dir", args.trie_dir]
+    if ref_built():
+        cmd.append("--with-ref-gpu")
+    t0 = time.time()
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=1200)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": "config 4 took more than 1200 s"}
+    child = None
+    for ln in r.stdout.splitlines()[::-1]:
+        if ln.startswith("{"):
+            child = json.loads(ln)
+            break
+    if child is None:
+        return {"unavailable": "config 4 exited %d: %s" % (r.returncode, r.stderr[-300:])}
+    keep = ("value", "unit", "ms_per_step", "config", "latency_ms", "e2e", "roofline", "clocks", "gpu_launches",
+            "results_per_request", "parity_vs_oracle", "reference_gpu")
+    out = {k: child[k] for k in keep if k in child}
+    out["setup_s"] = {k: child["setup_s"].get(k) for k in ("trie", "device_gb_image_and_workspace", "num_nodes",
+                                                         "num_keys")}
+    out["wall_s"] = round(time.time() - t0, 1)
+    out["what"] = ("north star: 800M-key, V=2.2M trie (config 4, the reference generator's key lengths), beam "
+                   "1000, batch 1, target p99 <= 1.5 ms; `python bench.py --config 4 --batch 1 --no-extras "
+                   "--cpu-budget 0 --with-ref-gpu` in a child process")
+    return out
 
 
 def main():
