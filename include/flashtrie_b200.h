@@ -209,8 +209,8 @@ int ft_trie_device_status(ft_trie *trie, uint32_t *status);
  * whose scratch would exceed 8 MiB are rejected with FT_ERR_INVALID_ARG.
  * The first call on a device looks up the array's address; make it before any
  * stream capture.  Calls are serialised per device; each reads the kernel's
- * status word back on `stream` and synchronises `stream` before it returns.
- * All calls share the array, so searches whose GPU work overlapped would race.
+ * status word back on `stream` and synchronises `stream` before it returns,
+ * so no call can be made inside a stream capture.  All calls share the array, so searches whose GPU work overlapped would race.
  */
 int ft_tbs_batch_device_noalloc(ft_trie *trie, const ft_device_batch *batch,
                                 const ft_search_params *params, void *stream);
