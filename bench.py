@@ -22,11 +22,13 @@ Arms:
              e2e = q/s through the drop-in `flashtrie.bs_tbs_gpu` with numpy
              host buffers (H2D of the inputs, D2H of the results inside the
              timed region).  Extra fields: latency by beam (100/500/1000,
-             batch 1), q/s at batch 8 (the reference's peak point) and at a
-             large batch with its roofline fraction, the total batch of 64
-             split over the N ranks (strong scaling), the reference kernel
-             (its sources compiled for sm_100a) on the same requests, and the
-             reference CPU `tbs` on one pinned core (cpu_baseline).
+             batch 1), q/s at batch 8 (the reference's peak point) and at
+             batches 296 and 1184 with the roofline fraction, the total batch
+             of 64 split over the N ranks (strong scaling), the reference
+             kernel (its sources compiled for sm_100a) on the same requests,
+             the reference CPU `tbs` on one pinned core (cpu_baseline), and on
+             one GPU the north star's point on config 4's 800M-key trie
+             (north_star, a child process).
   reference  the reference's CPU `tbs(use_gpu=False)` (the unmodified
              reference built from its sources by oracle/ref.mk), one worker
              process per host core, each pinned to its core; a step is one
